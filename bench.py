@@ -1,0 +1,398 @@
+"""Benchmark of the INT4-KV decode hot path (BASELINE config 2 per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (per rank): Llama-3.1-8B single-layer decode, B=16, 32 q heads,
+8 KV heads, d=128, context S=4096, INT4 group size 32, bf16 q/K/V, K
+channels scaled by log-uniform [0.5, 8] factors, seeded synthetic data.  A
+step = quantize-append of the new K/V token (one launch) + fused decode
+attention over the S-token INT4 cache, for one layer.  Steps rotate over 32
+layer caches (2.4 GB resident per GPU), so every step reads its cache from
+HBM, not L2 (126 MB).
+
+`value` = algorithmic bytes of all ranks' steps / max-over-ranks device time
+(GB/s).  `e2e` = the same metric through the public Python API with pinned
+host q/k/v copied in and the output copied out every step.  With N > 1 each
+rank owns its own batch shard (weak scaling, no collective on the data path).
+`--impl reference` times the reference's CPU formulation (oracle/torch_ref.py)
+on the host cores on a bounded batch sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "kv-cache-triton_b200"))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, S, D, G = 16, 32, 8, 4096, 128, 32
+LAYERS = 32
+METRIC = "INT4-KV decode attention HBM GB/s (Llama-3.1-8B shape, B16, S4096, G32)"
+
+
+def attn_bytes(b=B, hq=HQ, hkv=HKV, s=S, d=D, g=G, ss=2, qs=2):
+    """Algorithmic bytes of one decode-attention launch: packed K/V + scales
+    over the S-token cache, q read, output written."""
+    return 2 * b * hkv * s * (d // 2 + (d // g) * ss) + 2 * b * hq * d * qs
+
+
+def append_bytes(b=B, hkv=HKV, d=D, g=G, ss=2, xs=2):
+    return 2 * b * hkv * (d * xs + d // 2 + (d // g) * ss)
+
+
+STEP_BYTES = attn_bytes() + append_bytes()
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, index: int):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    _NAMES = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+              0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self._NAMES.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def build_caches(dev, seed=0):
+    from kvint4.cache import Int4KVStore
+    g = torch.Generator(device=dev).manual_seed(seed)
+    store = Int4KVStore(G, capacity=S)
+    fac = torch.exp(torch.empty(D, device=dev).uniform_(math.log(0.5), math.log(8.0),
+                                                        generator=g))
+    for layer in range(LAYERS):
+        k = (torch.randn(B, HKV, S, D, device=dev, generator=g) * fac).to(torch.bfloat16)
+        v = torch.randn(B, HKV, S, D, device=dev, generator=g).to(torch.bfloat16)
+        store.append(k, v, layer)
+        del k, v
+    q = torch.randn(LAYERS, B, HQ, 1, D, device=dev, generator=g).to(torch.bfloat16)
+    kn = (torch.randn(LAYERS, B, HKV, 1, D, device=dev, generator=g) * fac).to(torch.bfloat16)
+    vn = torch.randn(LAYERS, B, HKV, 1, D, device=dev, generator=g).to(torch.bfloat16)
+    return store, q, kn, vn
+
+
+def run_ours(args, ws, rank, local):
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    from kvint4 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    store, q, kn, vn = build_caches(dev, seed=rank)
+    out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def append_op(l):
+        layer = store.layer(l)
+        ops.append_kv(kn[l], vn[l], layer.k_packed_buf, layer.k_scales_buf, layer.v_packed_buf,
+                      layer.v_scales_buf, S - 1, G)  # the new token is row S-1: context stays S
+
+    def attn_op(l):
+        kp, ks, vp, vs = store.layer(l).views()
+        ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
+
+    for l in range(LAYERS):
+        store.layer(l).seq_len = S
+    p = ops.plan(q[0], *store.layer(0).views(), out, G, False)
+    # eager warm-up (caches occupancy queries / smem attributes), then one CUDA
+    # graph per (layer, op) so the timed loop is device-bound, not host-bound
+    for l in range(LAYERS):
+        append_op(l)
+        attn_op(l)
+    torch.cuda.synchronize()
+    g_app, g_att = [], []
+    for l in range(LAYERS):
+        ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga):
+            append_op(l)
+        with torch.cuda.graph(gb):
+            attn_op(l)
+        g_app.append(ga)
+        g_att.append(gb)
+    n_ev = args.warmup + args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n_ev)]
+
+    def step(i):
+        l = i % LAYERS
+        g_app[l].replay()
+        ev[i][0].record(st)
+        g_att[l].replay()
+        ev[i][1].record(st)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(st)
+        for i in range(args.warmup, args.warmup + args.steps):
+            step(i)
+        t1.record(st)
+        torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    attn_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.warmup, n_ev)]
+
+    # ---- e2e: public API, pinned host buffers in and out every step ----
+    hq = torch.randn(args.steps, B, HQ, 1, D).to(torch.bfloat16).pin_memory()
+    hk = torch.randn(args.steps, B, HKV, 1, D).to(torch.bfloat16).pin_memory()
+    hv = torch.randn(args.steps, B, HKV, 1, D).to(torch.bfloat16).pin_memory()
+    hout = torch.empty(args.steps, B, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
+    from models.llama3.kv_cache import QuantizedKVCache
+    caches = []
+    for l in range(LAYERS):
+        c = QuantizedKVCache(group_size=G)
+        c._store._layers[0] = store.layer(l)
+        caches.append(c)
+    dq = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+    dk = torch.empty(B, HKV, 1, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty_like(dk)
+
+    def e2e_step(i):
+        c = caches[i % LAYERS]
+        c._store.layer(0).seq_len = S - 1
+        dq.copy_(hq[i % args.steps], non_blocking=True)
+        dk.copy_(hk[i % args.steps], non_blocking=True)
+        dv.copy_(hv[i % args.steps], non_blocking=True)
+        c.append(dk, dv, 0)
+        kp, ks, vp, vs = c.get_quantized(0)
+        o = attention_forward_quant_gqa(dq, kp, ks, vp, vs, n_q_heads=HQ, n_kv_heads=HKV,
+                                        group_size=G)
+        hout[i % args.steps].copy_(o, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, statistics.mean(attn_ms)], device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.barrier()
+    ms, e2e_ms, attn_avg_ms = (float(x) for x in t.tolist())
+    if rank != 0:
+        return None
+    peak, peak_kind = _peaks()
+    per_step_ms = ms / args.steps
+    value = ws * STEP_BYTES * args.steps / (ms * 1e-3) / 1e9
+    achieved = attn_bytes() / (attn_avg_ms * 1e-3) / 1e9
+    h2d = (B * HQ * D + 2 * B * HKV * D) * 2
+    d2h = B * HQ * D * 2
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step_ms, 5),
+        "us_per_step": round(per_step_ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
+        "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
+        "config": {"workload": "llama3.1-8b single-layer decode: append 1 token + fused INT4 "
+                               "decode attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                   "seq_len": S, "d_head": D, "group_size": G,
+                   "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
+                   "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
+                         f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
+                   "bytes_per_step": STEP_BYTES},
+        "gpu_launches": args.steps * (1 + int(p.kernels)),
+        "e2e": {"value": round(ws * STEP_BYTES * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
+                "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast (+kv4_merge_slots)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": None},
+        "clocks": clk.summary(),
+        "plan": {"path": int(p.path), "ctas": int(p.ctas), "tiles_per_cta": int(p.tiles_per_cta),
+                 "kernels_per_attention": int(p.kernels)},
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    return line
+
+
+def cpu_baseline(budget_s: float = 15.0, batch_sample: int = 2):
+    """The reference's CPU formulation on a batch slice of config 2, all host threads."""
+    from oracle import torch_ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    fac = torch.exp(torch.empty(D).uniform_(math.log(0.5), math.log(8.0), generator=g))
+    k = (torch.randn(batch_sample, HKV, S - 1, D, generator=g) * fac).to(torch.bfloat16)
+    v = torch.randn(batch_sample, HKV, S - 1, D, generator=g).to(torch.bfloat16)
+    kp, ks = torch_ref.quantize_int4(k, G)
+    vp, vs = torch_ref.quantize_int4(v, G)
+    base = {"kp": kp, "ks": ks, "vp": vp, "vs": vs}
+    q = torch.randn(batch_sample, HQ, 1, D, generator=g).to(torch.bfloat16)
+    kn = torch.randn(batch_sample, HKV, 1, D, generator=g).to(torch.bfloat16)
+    vn = torch.randn(batch_sample, HKV, 1, D, generator=g).to(torch.bfloat16)
+    torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or n >= 200:
+            break
+    per_sample = el / n
+    frac = batch_sample / B
+    step_s = per_sample / frac
+    return {"value": round(STEP_BYTES / step_s / 1e9, 3), "unit": "GB/s",
+            "us_per_step": round(step_s * 1e6, 1), "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of batch {batch_sample}/{B} (S={S}) with the reference's "
+                      f"torch CPU path (quantize+cat+dequant+SDPA), scaled x{B // batch_sample}"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    from oracle import torch_ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    bs = 1
+    g = torch.Generator().manual_seed(0)
+    fac = torch.exp(torch.empty(D).uniform_(math.log(0.5), math.log(8.0), generator=g))
+    k = (torch.randn(bs, HKV, S - 1, D, generator=g) * fac).to(torch.bfloat16)
+    v = torch.randn(bs, HKV, S - 1, D, generator=g).to(torch.bfloat16)
+    kp, ks = torch_ref.quantize_int4(k, G)
+    vp, vs = torch_ref.quantize_int4(v, G)
+    base = {"kp": kp, "ks": ks, "vp": vp, "vs": vs}
+    q = torch.randn(bs, HQ, 1, D, generator=g).to(torch.bfloat16)
+    kn = torch.randn(bs, HKV, 1, D, generator=g).to(torch.bfloat16)
+    vn = torch.randn(bs, HKV, 1, D, generator=g).to(torch.bfloat16)
+    for _ in range(args.warmup):
+        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+    el = time.perf_counter() - t0
+    step_s = el / args.steps * (B / bs)  # per full config-2 step
+    value = STEP_BYTES / step_s / 1e9
+    sample = (f"each step = batch {bs}/{B} of config 2 (S={S}) through the reference's torch "
+              f"CPU path (quantize+cat+dequant+repeat_interleave+SDPA); rate scaled to the "
+              f"full batch")
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in, fp32 compute", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "llama3.1-8b single-layer decode: append 1 token + INT4 decode "
+                               "attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                   "seq_len": S, "d_head": D, "group_size": G},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        line = run_reference(args, ws, rank)
+    else:
+        line = run_ours(args, ws, rank, local)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if ws > 1 and args.impl == "ours":
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

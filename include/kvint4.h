@@ -1,0 +1,174 @@
+/*
+ * kvint4.h -- C ABI of libkvint4.so, the B200 (sm_100a) INT4 KV-cache library.
+ *
+ * Every entry point takes plain pointers, sizes and strides, returns an int
+ * status (KV4_OK == 0) and never throws.  Nothing here allocates device
+ * memory: outputs and any workspace are supplied by the caller.  All work is
+ * enqueued on the caller's CUDA stream (passed as `void *`, a cudaStream_t;
+ * NULL is the legacy default stream).
+ *
+ * Tensor arguments are described by kv4_tensor: a device pointer, a dtype
+ * code, a 4-D shape and 4-D strides counted in ELEMENTS of that dtype (for
+ * uint8 tensors elements are bytes).  Lower-rank tensors are passed with
+ * leading size-1 dimensions.
+ *
+ * Storage format (identical to the reference, johnchmura/kv-cache-triton):
+ *   packed  uint8 [..., ceil(d/G) * ceil(G/2)]  two 4-bit codes per byte,
+ *           low nibble = even column, high nibble = odd column, code = q + 8
+ *   scales  float [..., ceil(d/G)]  scale = max|x| / 7 over the group
+ *           (1.0 for an all-zero group); value = (code - 8) * scale
+ */
+#ifndef KVINT4_H
+#define KVINT4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+enum { KV4_F32 = 0, KV4_F16 = 1, KV4_BF16 = 2, KV4_U8 = 3 };
+
+/* rounding of x/scale to the integer code */
+enum {
+  KV4_TIE_HALF_AWAY = 0, /* floor(q+0.5) / ceil(q-0.5): the reference's Triton kernel
+                            (kernels/llama3/quantize.py:62-63) -- default */
+  KV4_TIE_HALF_EVEN = 1  /* torch.round: the reference's CPU path (kernels/llama3/quantize.py:139) */
+};
+
+/* status codes */
+enum {
+  KV4_OK = 0,
+  KV4_ERR_INVALID = 1,     /* bad argument value (group_size <= 0, heads not divisible, ...) */
+  KV4_ERR_DTYPE = 2,       /* unsupported dtype */
+  KV4_ERR_SHAPE = 3,       /* inconsistent shapes */
+  KV4_ERR_LAYOUT = 4,      /* strides/alignment the requested path cannot use */
+  KV4_ERR_WORKSPACE = 5,   /* workspace missing or too small */
+  KV4_ERR_CUDA = 6,        /* a CUDA runtime call failed (see kv4_last_cuda_error) */
+  KV4_ERR_UNSUPPORTED = 7, /* valid request outside what the library implements */
+  KV4_ERR_DEVICE = 8       /* a kernel reported a device-side error (bounded wait expired) */
+};
+
+typedef struct kv4_tensor {
+  void *data;
+  int32_t dtype;
+  int32_t pad_;
+  int64_t shape[4];
+  int64_t stride[4]; /* in elements */
+} kv4_tensor;
+
+/* Optional knobs for kv4_attention / kv4_attention_partial (pass NULL for defaults). */
+typedef struct kv4_attn_opts {
+  int32_t force_generic;   /* 1: use the generic (FFMA, any-stride) kernel */
+  int32_t tiles_per_cta;   /* >0: override the stream-K chunk (tiles of 64 tokens per CTA) */
+  int32_t max_ctas;        /* >0: cap the persistent grid */
+  int32_t reserved;
+} kv4_attn_opts;
+
+/* Launch plan report (filled by kv4_attention_plan). */
+typedef struct kv4_attn_plan {
+  int32_t path;            /* 1 = tensor-core TMA kernel, 2 = generic kernel */
+  int32_t ctas;            /* CTAs of the main kernel */
+  int32_t tiles_per_cta;   /* stream-K chunk (fast path) */
+  int32_t units;           /* (batch, kv head, column chunk) work units */
+  int32_t max_parts;       /* partial slots per unit */
+  int32_t kernels;         /* kernel launches one call makes (1 or 2) */
+  int64_t workspace_bytes; /* bytes the call needs in `workspace` */
+} kv4_attn_plan;
+
+/* Library version (major*10000 + minor*100 + patch) and a status message. */
+int kv4_version(void);
+const char *kv4_strerror(int status);
+/* Last CUDA error string recorded by a call that returned KV4_ERR_CUDA. */
+const char *kv4_last_cuda_error(void);
+
+/*
+ * Quantize x [n0, n1, n2, d] into packed [n0, n1, n2, >=pw] (uint8) and
+ * scales [n0, n1, n2, >=ng] (f32/f16/bf16), row (i0, i1, i2) written at
+ * packed/scales row (i0, i1, i2 + t_off).  x may be f32/f16/bf16 with any
+ * strides.  Codes use the un-rounded fp32 scale, IEEE division x/scale, and
+ * `tie_mode` rounding; the stored scale is rounded to the scales dtype.
+ * Replaces kernels/llama3/quantize.py:151-186 (_quantize_int4_triton) and
+ * kernels/gpt2/quantize.py:136-171.
+ */
+int kv4_quantize(const kv4_tensor *x, const kv4_tensor *packed, const kv4_tensor *scales,
+                 int64_t t_off, int group_size, int tie_mode, void *stream);
+
+/*
+ * Quantize-on-append of both K and V in ONE launch: k, v [B, Hkv, s_new, d]
+ * are quantized into the capacity buffers k_packed/v_packed [B, Hkv, cap, pw]
+ * and k_scales/v_scales [B, Hkv, cap, ng] at token rows [pos, pos + s_new).
+ * Replaces models/llama3/kv_cache.py:76-102 (quantize_int4 x2 + torch.cat x4)
+ * and models/gpt2/kv_cache.py:42-71.
+ */
+int kv4_append_kv(const kv4_tensor *k, const kv4_tensor *v, const kv4_tensor *k_packed,
+                  const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                  const kv4_tensor *v_scales, int64_t pos, int group_size, int tie_mode,
+                  void *stream);
+
+/*
+ * out[..., :d_out] = (code - 8) * scale, d_out = out->shape[3] (<= ng*G).
+ * Group slot width in nibbles is 2*packed_width/ng, as the reference's
+ * view() implies.  Replaces kernels/llama3/quantize.py:237-271 and
+ * kernels/gpt2/quantize.py:238-271.
+ */
+int kv4_dequantize(const kv4_tensor *packed, const kv4_tensor *scales, const kv4_tensor *out,
+                   int group_size, void *stream);
+
+/*
+ * Fused attention over the INT4 cache, dequantizing inside the kernel:
+ *   q [B, Hq, sq, d] (bf16/f16/f32), k_packed/v_packed [B, Hkv, sk, pw],
+ *   k_scales/v_scales [B, Hkv, sk, ng], out [B, Hq, sq, d] (dtype of q).
+ * Query head h reads KV head h / (Hq/Hkv); with is_causal, query row i sees
+ * keys j <= sk - sq + i (bottom-right).  sm_scale <= 0 means d^-1/2.
+ * `workspace` (device, >= kv4_attention_plan().workspace_bytes) holds
+ * split-sequence partials; it may be NULL when that size is 0.
+ * Replaces kernels/llama3/attention_quant.py:159-286
+ * (attention_forward_quant_gqa) and kernels/gpt2/attention_quant.py:140-248
+ * (attention_forward_quant, Hq == Hkv).
+ */
+int kv4_attention(const kv4_tensor *q, const kv4_tensor *k_packed, const kv4_tensor *k_scales,
+                  const kv4_tensor *v_packed, const kv4_tensor *v_scales, const kv4_tensor *out,
+                  int group_size, int is_causal, float sm_scale, void *workspace,
+                  size_t workspace_bytes, const kv4_attn_opts *opts, void *stream);
+
+/* Plan (path, grid, workspace size) of kv4_attention for the same arguments. */
+int kv4_attention_plan(const kv4_tensor *q, const kv4_tensor *k_packed,
+                       const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                       const kv4_tensor *v_scales, const kv4_tensor *out, int group_size,
+                       int is_causal, const kv4_attn_opts *opts, kv4_attn_plan *plan);
+
+/*
+ * Sequence-shard partial of kv4_attention (new; the reference has no
+ * multi-GPU layer, it relies on accelerate device_map placement,
+ * benchmarks/llama3/run_llama3_benchmark.py:115-121).  The cache slice holds
+ * global key positions [k_offset, k_offset + sk) of a sequence of sk_total
+ * keys.  Writes part_o [B, Hq, sq, d] (f32, normalised within the shard) and
+ * part_lse [B, Hq, sq, 1] (f32, natural-log sum of exp of the scaled scores;
+ * -inf where the shard holds no visible key).
+ */
+int kv4_attention_partial(const kv4_tensor *q, const kv4_tensor *k_packed,
+                          const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                          const kv4_tensor *v_scales, const kv4_tensor *part_o,
+                          const kv4_tensor *part_lse, int64_t k_offset, int64_t sk_total,
+                          int group_size, int is_causal, float sm_scale, void *workspace,
+                          size_t workspace_bytes, const kv4_attn_opts *opts, void *stream);
+
+/*
+ * Log-sum-exp merge of n_parts shard partials: parts_o f32 contiguous
+ * [n_parts, rows, d], parts_lse f32 contiguous [n_parts, rows];
+ * out [B, Hq, sq, d] with B*Hq*sq == rows (any float dtype, any strides).
+ * The merge step of the sequence-sharded multi-GPU decode (new layer).
+ */
+int kv4_lse_combine(const float *parts_o, const float *parts_lse, int64_t n_parts,
+                    const kv4_tensor *out, void *stream);
+
+/* Read-and-clear the device error word that bounded waits set (synchronizes the stream). */
+int kv4_device_error(void *stream, int *flag_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVINT4_H */

@@ -1,0 +1,1163 @@
+// Fused attention over the packed INT4 KV cache (decode and short multi-query).
+//
+// Semantics follow kernels/llama3/attention_quant.py:24-152 of the reference:
+//   out[b, h, i] = softmax_j(q[b,h,i] . K[b, h/R, j] * sm_scale) . V[b, h/R, j]
+// with K/V = (code - 8) * scale dequantized inside the kernel, R = Hq/Hkv,
+// and (is_causal) keys j <= sk - sq + i visible (bottom-right alignment).
+//
+// Two device paths:
+//  * fast (kv4_attn_fast): one CTA = 4 warps streams 64-token tiles of packed
+//    K/V + scales from HBM into shared memory with TMA (cp.async.bulk.tensor,
+//    64B/128B/32B swizzle, no multicast), several stages deep.  All q heads of
+//    a GQA group (and all query rows, up to 8 columns per CTA) share ONE read
+//    of the group's KV.  Scores and P.V run on the tensor cores
+//    (mma.m16n8k16 bf16 -> fp32) with the packed nibbles turned into bf16
+//    operands in registers; per-group scales are applied exactly in fp32
+//    (K: after a per-group partial dot product; V: folded into P).  The grid
+//    is persistent and stream-K balanced over (unit, token tile) work;
+//    units split across CTAs leave (o, lse) partials that a second small
+//    kernel merges with a log-sum-exp reduction.
+//  * generic (kv4_attn_generic): a warp-per-token FFMA kernel for any shape,
+//    dtype, stride, group size and long query blocks.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace kv4 {
+
+// device error word written by bounded waits (read and cleared by kv4_device_error)
+static __device__ int g_device_error = 0;
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kNegInf = -INFINITY;
+
+// Output modes of both paths
+enum OutMode : int { OUT_FINAL = 0, OUT_PARTIAL = 1 };
+
+struct AttnCommon {
+  const void *q;
+  int64_t qs[4];
+  int q_dtype;
+  void *out;  // OUT_FINAL: [B,Hq,sq,d] in out_dtype ; OUT_PARTIAL: part_o f32
+  int64_t os[4];
+  int out_dtype;
+  float *lse;  // OUT_PARTIAL: part_lse f32 [B,Hq,sq]
+  int64_t ls[3];
+  int mode;
+  int B, Hq, Hkv, R, sq, sk, d, G;
+  int causal;
+  int64_t k_offset, sk_total;  // global key positions of this cache slice
+  float scale_log2;            // sm_scale * log2(e)
+};
+
+// visible-key limit (exclusive, local index) of query row qi
+__device__ __forceinline__ int64_t key_limit(const AttnCommon &C, int qi) {
+  if (!C.causal) return C.sk;
+  int64_t lim = C.sk_total - C.sq + qi + 1 - C.k_offset;
+  return lim < C.sk ? lim : C.sk;
+}
+
+// write one finished (m, l, o) row: o_unnorm/l to out (FINAL) or (o, lse) to partials
+__device__ __forceinline__ void emit_value(const AttnCommon &C, int b, int h, int qi, int dd,
+                                           float val) {
+  const int64_t off = b * C.os[0] + h * C.os[1] + qi * C.os[2] + dd * C.os[3];
+  if (C.mode == OUT_FINAL) store_from_f32(C.out, C.out_dtype, off, val);
+  else static_cast<float *>(C.out)[off] = val;
+}
+__device__ __forceinline__ void emit_lse(const AttnCommon &C, int b, int h, int qi,
+                                         float lse_log2) {
+  if (C.mode != OUT_PARTIAL) return;
+  C.lse[b * C.ls[0] + h * C.ls[1] + qi * C.ls[2]] = lse_log2 * kLn2;
+}
+
+// ===========================================================================
+// generic path
+// ===========================================================================
+struct GenParams {
+  AttnCommon c;
+  const uint8_t *kp, *vp;
+  const void *ks, *vs;
+  int64_t kps[4], vps[4], kss[4], vss[4];
+  int s_dtype;
+};
+
+__device__ __forceinline__ float deq(const uint8_t *p, const int64_t *ps, const void *s,
+                                     const int64_t *ss, int sdt, int64_t base_p,
+                                     int64_t base_s, int dd, int G) {
+  const uint8_t byte = p[base_p + (dd >> 1) * ps[3]];
+  const int code = (dd & 1) ? (byte >> 4) : (byte & 15);
+  return static_cast<float>(code - 8) * load_as_f32(s, sdt, base_s + (dd / G) * ss[3]);
+}
+
+template <int NDI>
+__global__ void __launch_bounds__(128) kv4_attn_generic(const GenParams P) {
+  const AttnCommon &C = P.c;
+  const int bh = blockIdx.x;
+  const int b = bh / C.Hq, h = bh % C.Hq;
+  const int qi = blockIdx.y;
+  const int kvh = h / C.R;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NW = 4;
+
+  float qv[NDI], acc[NDI];
+#pragma unroll
+  for (int i = 0; i < NDI; ++i) {
+    const int dd = lane + 32 * i;
+    qv[i] = dd < C.d ? load_as_f32(C.q, C.q_dtype,
+                                   b * C.qs[0] + h * C.qs[1] + qi * C.qs[2] + dd * C.qs[3])
+                     : 0.0f;
+    acc[i] = 0.0f;
+  }
+  float m = kNegInf, l = 0.0f;
+  const int64_t lim = key_limit(C, qi);
+  for (int64_t t = warp; t < lim; t += NW) {
+    const int64_t bpk = b * P.kps[0] + kvh * P.kps[1] + t * P.kps[2];
+    const int64_t bsk = b * P.kss[0] + kvh * P.kss[1] + t * P.kss[2];
+    float part = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NDI; ++i) {
+      const int dd = lane + 32 * i;
+      if (dd < C.d) part += qv[i] * deq(P.kp, P.kps, P.ks, P.kss, P.s_dtype, bpk, bsk, dd, C.G);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const float s = part * C.scale_log2;
+    const float mn = fmaxf(m, s);
+    const float alpha = exp2f(m - mn);  // m == -inf -> 0
+    const float p = exp2f(s - mn);
+    l = l * alpha + p;
+    const int64_t bpv = b * P.vps[0] + kvh * P.vps[1] + t * P.vps[2];
+    const int64_t bsv = b * P.vss[0] + kvh * P.vss[1] + t * P.vss[2];
+#pragma unroll
+    for (int i = 0; i < NDI; ++i) {
+      const int dd = lane + 32 * i;
+      const float vv =
+          dd < C.d ? deq(P.vp, P.vps, P.vs, P.vss, P.s_dtype, bpv, bsv, dd, C.G) : 0.0f;
+      acc[i] = acc[i] * alpha + p * vv;
+    }
+    m = mn;
+  }
+  // merge the 4 warps
+  __shared__ float sm_m[NW], sm_l[NW];
+  __shared__ float sm_o[NW][NDI * 32];
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = l;
+  }
+#pragma unroll
+  for (int i = 0; i < NDI; ++i) sm_o[warp][lane + 32 * i] = acc[i];
+  __syncthreads();
+  float M = kNegInf;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w]);
+  float L = 0.0f, f[NW];
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    f[w] = (M == kNegInf) ? 0.0f : exp2f(sm_m[w] - M);
+    L += sm_l[w] * f[w];
+  }
+  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+  for (int dd = threadIdx.x; dd < C.d; dd += blockDim.x) {
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) o += sm_o[w][dd] * f[w];
+    emit_value(C, b, h, qi, dd, o * inv);
+  }
+  if (threadIdx.x == 0) emit_lse(C, b, h, qi, L > 0.0f ? M + log2f(L) : kNegInf);
+}
+
+// ===========================================================================
+// fast path
+// ===========================================================================
+constexpr int TOK = 64;    // tokens per pipeline stage (4 warps x 16 rows)
+constexpr int NWARP = 4;
+constexpr int NCOL = 8;    // (head, query row) columns per CTA = MMA N
+
+struct FastParams {
+  AttnCommon c;
+  int ncols;      // R * sq
+  int hc;         // column chunks per (b, kvh)
+  int tpu;        // tiles per unit
+  int L;          // tiles per CTA (stream-K chunk)
+  int64_t total_tiles;
+  int maxp;       // partial slots per unit
+  float *ws_o;    // [units*maxp][NCOL][d]
+  float *ws_lse;  // [units*maxp][NCOL]   (log2 domain)
+};
+
+template <int D, int G, typename ST>
+struct FastCfg {
+  static constexpr int P = D / 2;             // packed bytes per token
+  static constexpr int NCH = D / 32;          // 16-byte chunks per token row
+  static constexpr int NG = D / G;            // scale groups per token
+  static constexpr int CPG = G / 32;          // chunks per group
+  static constexpr int SROW = NG * (int)sizeof(ST);  // scale bytes per token
+  static constexpr int KP = TOK * P;          // packed bytes per stage per tensor
+  static constexpr int KS = TOK * SROW;       // scale bytes per stage per tensor
+  static constexpr int TS = (TOK * NG <= 256) ? TOK : 256 / NG;  // tokens per scale TMA box
+  static constexpr int NSB = TOK / TS;        // scale boxes per stage per tensor
+  static constexpr int STAGE = ((2 * KP + 2 * KS) + 1023) / 1024 * 1024;
+  static constexpr int STAGES = (D == 256) ? 3 : 4;
+  static constexpr int SWZ = (P == 32) ? 1 : (P == 64) ? 3 : 7;
+  static constexpr int MERGE = NWARP * NCOL * D * 4;
+  static constexpr int SMEM = STAGES * STAGE + MERGE + 2 * NWARP * NCOL * 4 + 64 + 1024;
+  static constexpr uint32_t TX = 2 * KP + 2 * KS;
+};
+
+// physical byte offset of logical offset o in a TMA-swizzled [TOK][P] tile
+template <int SWZ>
+__device__ __forceinline__ uint32_t swz(uint32_t o) {
+  return o ^ (((o >> 7) & SWZ) << 4);
+}
+
+// nibble extraction into bf16x2 "128 + code" values (exact): low nibbles of
+// bytes 0 and 2 of x land in the low and high halves.
+__device__ __forceinline__ uint32_t nib2(uint32_t x) { return (x & 0x000F000Fu) | 0x43004300u; }
+
+template <typename ST>
+__device__ __forceinline__ void load_scales(uint32_t addr, float (&s)[8], int ng);
+
+template <int NG, typename ST>
+__device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
+  if constexpr (sizeof(ST) == 2) {
+    if constexpr (NG == 1) {
+      uint32_t w = lds16(addr);
+      s[0] = to_f32(*reinterpret_cast<const ST *>(&w));
+    } else if constexpr (NG == 2) {
+      uint32_t w = lds32(addr);
+      const ST *h = reinterpret_cast<const ST *>(&w);
+      s[0] = to_f32(h[0]); s[1] = to_f32(h[1]);
+    } else if constexpr (NG == 4) {
+      uint2 w = lds64(addr);
+      const ST *h = reinterpret_cast<const ST *>(&w);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i] = to_f32(h[i]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NG / 8; ++k) {
+        uint4 w = lds128(addr + 16 * k);
+        const ST *h = reinterpret_cast<const ST *>(&w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[8 * k + i] = to_f32(h[i]);
+      }
+    }
+  } else {
+    if constexpr (NG == 1) {
+      s[0] = __uint_as_float(lds32(addr));
+    } else if constexpr (NG == 2) {
+      uint2 w = lds64(addr);
+      s[0] = __uint_as_float(w.x); s[1] = __uint_as_float(w.y);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NG / 4; ++k) {
+        uint4 w = lds128(addr + 16 * k);
+        s[4 * k + 0] = __uint_as_float(w.x); s[4 * k + 1] = __uint_as_float(w.y);
+        s[4 * k + 2] = __uint_as_float(w.z); s[4 * k + 3] = __uint_as_float(w.w);
+      }
+    }
+  }
+}
+
+template <int D, int G, typename ST, bool SPLIT>
+__global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
+    kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
+                  const __grid_constant__ CUtensorMap tm_vp,
+                  const __grid_constant__ CUtensorMap tm_ks,
+                  const __grid_constant__ CUtensorMap tm_vs) {
+  using Cfg = FastCfg<D, G, ST>;
+  constexpr int NCH = Cfg::NCH, NG = Cfg::NG, CPG = Cfg::CPG;
+  const AttnCommon &C = P.c;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float *merge_o = reinterpret_cast<float *>(smem + Cfg::STAGES * Cfg::STAGE);
+  float *merge_m = merge_o + NWARP * NCOL * D;
+  float *merge_l = merge_m + NWARP * NCOL;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(merge_l + NWARP * NCOL);
+  __shared__ int sh_abort;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tg = lane & 3;
+
+  const int64_t first_tile = static_cast<int64_t>(blockIdx.x) * P.L;
+  const int64_t last_tile = min(first_tile + P.L, P.total_tiles);  // exclusive
+  const int ntiles = static_cast<int>(last_tile - first_tile);
+  if (ntiles <= 0) return;
+
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t bar_base = smem_u32(bars);
+
+  if (tid == 0) {
+    sh_abort = 0;
+    prefetch_tmap(&tm_kp);
+    prefetch_tmap(&tm_vp);
+    prefetch_tmap(&tm_ks);
+    prefetch_tmap(&tm_vs);
+    for (int s = 0; s < Cfg::STAGES; ++s) mbar_init(bar_base + 8 * s, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // unit -> (b, kvh, column chunk)
+  auto unit_of = [&](int64_t gt) { return static_cast<int>(gt / P.tpu); };
+
+  auto issue = [&](int i) {  // local tile i -> stage i % STAGES
+    const int64_t gt = first_tile + i;
+    const int u = unit_of(gt);
+    const int ti = static_cast<int>(gt - static_cast<int64_t>(u) * P.tpu);
+    const int bk = u / P.hc;
+    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+    const int t0 = ti * TOK;
+    const int s = i % Cfg::STAGES;
+    const uint32_t bar = bar_base + 8 * s;
+    const uint32_t dst = smem_base + s * Cfg::STAGE;
+    mbar_arrive_expect_tx(bar, Cfg::TX);
+    tma_load_4d(dst, &tm_kp, bar, 0, t0, kvh, b);
+    tma_load_4d(dst + Cfg::KP, &tm_vp, bar, 0, t0, kvh, b);
+#pragma unroll
+    for (int k = 0; k < Cfg::NSB; ++k) {
+      const int x = (t0 + k * Cfg::TS) * NG;
+      tma_load_3d(dst + 2 * Cfg::KP + k * Cfg::TS * Cfg::SROW, &tm_ks, bar, x, kvh, b);
+      tma_load_3d(dst + 2 * Cfg::KP + Cfg::KS + k * Cfg::TS * Cfg::SROW, &tm_vs, bar, x, kvh,
+                  b);
+    }
+  };
+
+  if (tid == 0) {
+    const int pre = min(ntiles, Cfg::STAGES);
+    for (int i = 0; i < pre; ++i) issue(i);
+  }
+
+  // ---- per-unit state --------------------------------------------------
+  uint32_t qf[NCH][2][2];       // q B-fragments (hi), [chunk][kstep][reg]
+  uint32_t qfl[SPLIT ? NCH : 1][2][2];  // lo parts (SPLIT only)
+  float bias[NG][2];            // -136 * sum(q) per group for cols 2tg, 2tg+1
+  float o_acc[NCH][2][4];       // O^T fragments [chunk][j][c]
+  float sp_acc[NG][4];          // sum of P' per group (for the +128 bias of V codes)
+  float m_run[2], l_run[2];
+  int cur_unit = -1;
+  int col_qi[2];                // query row of this lane's columns 2tg, 2tg+1
+  int64_t col_lim[2];
+
+  auto load_unit = [&](int u) {
+    const int bk = u / P.hc, hcid = u % P.hc;
+    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+    // B operand column n = g
+    {
+      const int n = hcid * NCOL + g;
+      const bool ok = n < P.ncols;
+      const int qi = ok ? n / C.R : 0;
+      const int hl = ok ? n % C.R : 0;
+      const int h = kvh * C.R + hl;
+      const int64_t qbase = b * C.qs[0] + h * C.qs[1] + qi * C.qs[2];
+      float gsum[NG];
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) gsum[gi] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float v[8], hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int dd = 32 * c + 8 * tg + e;
+          v[e] = ok ? load_as_f32(C.q, C.q_dtype, qbase + dd * C.qs[3]) : 0.0f;
+          hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+          lo[e] = SPLIT ? __bfloat162float(__float2bfloat16_rn(v[e] - hi[e])) : 0.0f;
+          gsum[c / CPG] += hi[e] + lo[e];
+        }
+        // k-step 0: (b0,b1) <- dims (0,4) ; (b2,b3) <- dims (1,5)
+        // k-step 1: (b0,b1) <- dims (2,6) ; (b2,b3) <- dims (3,7)
+        qf[c][0][0] = pack_bf16x2(hi[0], hi[4]);
+        qf[c][0][1] = pack_bf16x2(hi[1], hi[5]);
+        qf[c][1][0] = pack_bf16x2(hi[2], hi[6]);
+        qf[c][1][1] = pack_bf16x2(hi[3], hi[7]);
+        if constexpr (SPLIT) {
+          qfl[c][0][0] = pack_bf16x2(lo[0], lo[4]);
+          qfl[c][0][1] = pack_bf16x2(lo[1], lo[5]);
+          qfl[c][1][0] = pack_bf16x2(lo[2], lo[6]);
+          qfl[c][1][1] = pack_bf16x2(lo[3], lo[7]);
+        }
+      }
+      // reduce the per-group sums over the 4 lanes of the quad (tg)
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        gsum[gi] += __shfl_xor_sync(0xffffffffu, gsum[gi], 1);
+        gsum[gi] += __shfl_xor_sync(0xffffffffu, gsum[gi], 2);
+      }
+      // lane (g, tg) now holds column g's sums; fetch columns 2tg, 2tg+1
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        const float s0 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg) * 4);
+        const float s1 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg + 1) * 4);
+        bias[gi][0] = -136.0f * s0;
+        bias[gi][1] = -136.0f * s1;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = hcid * NCOL + 2 * tg + j;
+      const int qi = n < P.ncols ? n / C.R : 0;
+      col_qi[j] = qi;
+      col_lim[j] = n < P.ncols ? key_limit(C, qi) : 0;
+      m_run[j] = kNegInf;
+      l_run[j] = 0.0f;
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o_acc[c][j][e] = 0.0f;
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sp_acc[gi][e] = 0.0f;
+  };
+
+  // finish the current unit segment: merge warps through smem, write output
+  auto flush = [&](int u) {
+    const int bk = u / P.hc, hcid = u % P.hc;
+    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+    // l over the 8 token-row lanes
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
+    }
+    if (g == 0) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        merge_m[warp * NCOL + 2 * tg + j] = m_run[j];
+        merge_l[warp * NCOL + 2 * tg + j] = l_run[j];
+      }
+    }
+    // O^T fragment -> smem [warp][col][dim]; remove the +128 code bias
+    float *mo = merge_o + warp * NCOL * D;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int gi = c / CPG;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int d0 = 32 * c + 4 * g + 2 * j;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {  // column 2tg + cc
+          const float corr = 136.0f * sp_acc[gi][cc];
+          mo[(2 * tg + cc) * D + d0] = o_acc[c][j][cc] - corr;
+          mo[(2 * tg + cc) * D + d0 + 1] = o_acc[c][j][2 + cc] - corr;
+        }
+      }
+    }
+    __syncthreads();
+    const int64_t ft = static_cast<int64_t>(u) * P.tpu;
+    const int first_cta = static_cast<int>(ft / P.L);
+    const int last_cta = static_cast<int>((ft + P.tpu - 1) / P.L);
+    const bool whole = first_cta == last_cta;
+    const int slot = u * P.maxp + (static_cast<int>(blockIdx.x) - first_cta);
+    for (int idx = tid; idx < NCOL * D; idx += blockDim.x) {
+      const int col = idx / D, dd = idx % D;
+      const int n = hcid * NCOL + col;
+      if (n >= P.ncols) continue;
+      float M = kNegInf;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) M = fmaxf(M, merge_m[w * NCOL + col]);
+      float Lsum = 0.0f, o = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) {
+        const float f = (M == kNegInf) ? 0.0f : exp2f(merge_m[w * NCOL + col] - M);
+        Lsum += merge_l[w * NCOL + col] * f;
+        o += merge_o[(w * NCOL + col) * D + dd] * f;
+      }
+      const float val = Lsum > 0.0f ? o / Lsum : 0.0f;
+      const float lse = Lsum > 0.0f ? M + log2f(Lsum) : kNegInf;
+      const int qi = n / C.R, h = kvh * C.R + n % C.R;
+      if (whole) {
+        emit_value(C, b, h, qi, dd, val);
+        if (dd == 0) emit_lse(C, b, h, qi, lse);
+      } else {
+        P.ws_o[(static_cast<int64_t>(slot) * NCOL + col) * D + dd] = val;
+        if (dd == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = lse;
+      }
+    }
+    __syncthreads();
+  };
+
+  const uint32_t ones = 0x3F803F80u;  // bf16x2 (1, 1)
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int64_t gt = first_tile + i;
+    const int u = unit_of(gt);
+    const int ti = static_cast<int>(gt - static_cast<int64_t>(u) * P.tpu);
+    if (u != cur_unit) {
+      load_unit(u);
+      cur_unit = u;
+    }
+    const int s = i % Cfg::STAGES;
+    const uint32_t phase = (i / Cfg::STAGES) & 1;
+    if (!mbar_wait_bounded(bar_base + 8 * s, phase)) {
+      atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
+      sh_abort = 1;
+    }
+    const uint32_t kp = smem_base + s * Cfg::STAGE;
+    const uint32_t vp = kp + Cfg::KP;
+    const uint32_t ksb = kp + 2 * Cfg::KP;
+    const uint32_t vsb = ksb + Cfg::KS;
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    const int tok0 = ti * TOK;
+
+    // ---------------- scores: S^T[token][col] ---------------------------
+    float sc[NG][4];
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      sc[gi][0] = bias[gi][0];
+      sc[gi][1] = bias[gi][1];
+      sc[gi][2] = bias[gi][0];
+      sc[gi][3] = bias[gi][1];
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t x0 = lds32(kp + swz<Cfg::SWZ>(r0 * Cfg::P + 16 * c + 4 * tg));
+      const uint32_t x1 = lds32(kp + swz<Cfg::SWZ>(r1 * Cfg::P + 16 * c + 4 * tg));
+      const int gi = c / CPG;
+      mma_bf16_16816(sc[gi], nib2(x0), nib2(x1), nib2(x0 >> 4), nib2(x1 >> 4), qf[c][0][0],
+                     qf[c][0][1]);
+      mma_bf16_16816(sc[gi], nib2(x0 >> 8), nib2(x1 >> 8), nib2(x0 >> 12), nib2(x1 >> 12),
+                     qf[c][1][0], qf[c][1][1]);
+      if constexpr (SPLIT) {
+        mma_bf16_16816(sc[gi], nib2(x0), nib2(x1), nib2(x0 >> 4), nib2(x1 >> 4), qfl[c][0][0],
+                       qfl[c][0][1]);
+        mma_bf16_16816(sc[gi], nib2(x0 >> 8), nib2(x1 >> 8), nib2(x0 >> 12), nib2(x1 >> 12),
+                       qfl[c][1][0], qfl[c][1][1]);
+      }
+    }
+    float ks0[NG], ks1[NG], vs0[NG], vs1[NG];
+    scales_row<NG, ST>(ksb + r0 * Cfg::SROW, ks0);
+    scales_row<NG, ST>(ksb + r1 * Cfg::SROW, ks1);
+    scales_row<NG, ST>(vsb + r0 * Cfg::SROW, vs0);
+    scales_row<NG, ST>(vsb + r1 * Cfg::SROW, vs1);
+    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;  // [row r0/r1][col 2tg / 2tg+1]
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      s00 = fmaf(ks0[gi], sc[gi][0], s00);
+      s01 = fmaf(ks0[gi], sc[gi][1], s01);
+      s10 = fmaf(ks1[gi], sc[gi][2], s10);
+      s11 = fmaf(ks1[gi], sc[gi][3], s11);
+    }
+    s00 *= C.scale_log2; s01 *= C.scale_log2; s10 *= C.scale_log2; s11 *= C.scale_log2;
+    {
+      const int64_t t_r0 = tok0 + r0, t_r1 = tok0 + r1;
+      if (t_r0 >= col_lim[0]) s00 = kNegInf;
+      if (t_r0 >= col_lim[1]) s01 = kNegInf;
+      if (t_r1 >= col_lim[0]) s10 = kNegInf;
+      if (t_r1 >= col_lim[1]) s11 = kNegInf;
+    }
+    // ---------------- online softmax (per column, lazy rescale) ---------
+    float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+#pragma unroll
+    for (int o = 4; o <= 16; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const bool need = (mx0 > m_run[0] + 8.0f) || (mx1 > m_run[1] + 8.0f);
+    if (__any_sync(0xffffffffu, need)) {
+      float alpha[2];
+      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+      alpha[0] = (mn0 == kNegInf) ? 1.0f : fast_exp2(m_run[0] - mn0);
+      alpha[1] = (mn1 == kNegInf) ? 1.0f : fast_exp2(m_run[1] - mn1);
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+      l_run[0] *= alpha[0];
+      l_run[1] *= alpha[1];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          o_acc[c][j][0] *= alpha[0];
+          o_acc[c][j][1] *= alpha[1];
+          o_acc[c][j][2] *= alpha[0];
+          o_acc[c][j][3] *= alpha[1];
+        }
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        sp_acc[gi][0] *= alpha[0];
+        sp_acc[gi][1] *= alpha[1];
+        sp_acc[gi][2] *= alpha[0];
+        sp_acc[gi][3] *= alpha[1];
+      }
+    }
+    const float me0 = (m_run[0] == kNegInf) ? 0.0f : m_run[0];
+    const float me1 = (m_run[1] == kNegInf) ? 0.0f : m_run[1];
+    const float p00 = fast_exp2(s00 - me0), p01 = fast_exp2(s01 - me1);
+    const float p10 = fast_exp2(s10 - me0), p11 = fast_exp2(s11 - me1);
+    l_run[0] += p00 + p10;
+    l_run[1] += p01 + p11;
+
+    // ---------------- P' = P * v_scale per group, as B fragments --------
+    uint32_t pb[NG][2];
+    uint32_t pbl[SPLIT ? NG : 1][2];
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      const float a0 = p00 * vs0[gi], a1 = p01 * vs0[gi];
+      const float c0 = p10 * vs1[gi], c1 = p11 * vs1[gi];
+      const uint32_t u0 = pack_bf16x2(a0, a1);
+      const uint32_t u1 = pack_bf16x2(c0, c1);
+      pb[gi][0] = movmatrix_trans(u0);
+      pb[gi][1] = movmatrix_trans(u1);
+      if constexpr (SPLIT) {
+        const uint32_t l0 = pack_bf16x2(a0 - bf16lo_to_f32(u0), a1 - bf16hi_to_f32(u0));
+        const uint32_t l1 = pack_bf16x2(c0 - bf16lo_to_f32(u1), c1 - bf16hi_to_f32(u1));
+        pbl[gi][0] = movmatrix_trans(l0);
+        pbl[gi][1] = movmatrix_trans(l1);
+      }
+    }
+    // ---------------- O^T[dim][col] += V^T . P' -------------------------
+    const int ra = 16 * warp + 2 * tg;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t ha = lds16(vp + swz<Cfg::SWZ>(ra * Cfg::P + 16 * c + 2 * g));
+      const uint32_t hb = lds16(vp + swz<Cfg::SWZ>((ra + 1) * Cfg::P + 16 * c + 2 * g));
+      const uint32_t hc = lds16(vp + swz<Cfg::SWZ>((ra + 8) * Cfg::P + 16 * c + 2 * g));
+      const uint32_t hd = lds16(vp + swz<Cfg::SWZ>((ra + 9) * Cfg::P + 16 * c + 2 * g));
+      const uint32_t wab = prmt(ha, hb, 0x5410);
+      const uint32_t wcd = prmt(hc, hd, 0x5410);
+      const int gi = c / CPG;
+      mma_bf16_16816(o_acc[c][0], nib2(wab), nib2(wab >> 4), nib2(wcd), nib2(wcd >> 4),
+                     pb[gi][0], pb[gi][1]);
+      mma_bf16_16816(o_acc[c][1], nib2(wab >> 8), nib2(wab >> 12), nib2(wcd >> 8),
+                     nib2(wcd >> 12), pb[gi][0], pb[gi][1]);
+      if constexpr (SPLIT) {
+        mma_bf16_16816(o_acc[c][0], nib2(wab), nib2(wab >> 4), nib2(wcd), nib2(wcd >> 4),
+                       pbl[gi][0], pbl[gi][1]);
+        mma_bf16_16816(o_acc[c][1], nib2(wab >> 8), nib2(wab >> 12), nib2(wcd >> 8),
+                       nib2(wcd >> 12), pbl[gi][0], pbl[gi][1]);
+      }
+    }
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
+      if constexpr (SPLIT)
+        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pbl[gi][0], pbl[gi][1]);
+    }
+
+    // ---------------- release the stage, refill, flush at unit end ------
+    __syncthreads();
+    if (sh_abort) break;
+    if (tid == 0 && i + Cfg::STAGES < ntiles) issue(i + Cfg::STAGES);
+    const bool unit_end = (ti == P.tpu - 1) || (i == ntiles - 1);
+    if (unit_end) flush(u);
+  }
+  if (sh_abort && tid == 0) {
+    // drain: wait (bounded) for every load this CTA may still have in flight
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % Cfg::STAGES;
+      mbar_wait_bounded(bar_base + 8 * s, (i / Cfg::STAGES) & 1, 1u << 16);
+    }
+  }
+}
+
+// ===========================================================================
+// merge of stream-K partials (within one launch) and of shard partials
+// ===========================================================================
+__global__ void __launch_bounds__(128) kv4_merge_slots(const FastParams P) {
+  const AttnCommon &C = P.c;
+  const int u = blockIdx.x;
+  const int col = blockIdx.y;
+  const int D = C.d;
+  const int64_t ft = static_cast<int64_t>(u) * P.tpu;
+  const int first_cta = static_cast<int>(ft / P.L);
+  const int last_cta = static_cast<int>((ft + P.tpu - 1) / P.L);
+  if (first_cta == last_cta) return;
+  const int bk = u / P.hc, hcid = u % P.hc;
+  const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+  const int n = hcid * NCOL + col;
+  if (n >= P.ncols) return;
+  const int nparts = last_cta - first_cta + 1;
+  const int64_t slot0 = static_cast<int64_t>(u) * P.maxp;
+  float M = kNegInf;
+  for (int p = 0; p < nparts; ++p) M = fmaxf(M, P.ws_lse[(slot0 + p) * NCOL + col]);
+  float W = 0.0f;
+  for (int p = 0; p < nparts; ++p) {
+    const float lp = P.ws_lse[(slot0 + p) * NCOL + col];
+    W += (M == kNegInf) ? 0.0f : exp2f(lp - M);
+  }
+  const float invW = W > 0.0f ? 1.0f / W : 0.0f;
+  const int qi = n / C.R, h = kvh * C.R + n % C.R;
+  for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
+    float o = 0.0f;
+    for (int p = 0; p < nparts; ++p) {
+      const float lp = P.ws_lse[(slot0 + p) * NCOL + col];
+      const float w = (M == kNegInf) ? 0.0f : exp2f(lp - M);
+      o += w * P.ws_o[((slot0 + p) * NCOL + col) * D + dd];
+    }
+    emit_value(C, b, h, qi, dd, o * invW);
+  }
+  if (threadIdx.x == 0) emit_lse(C, b, h, qi, W > 0.0f ? M + log2f(W) : kNegInf);
+}
+
+struct LseParams {
+  const float *po;
+  const float *pl;
+  int64_t nparts, rows;
+  int d;
+  void *out;
+  int64_t os[4];
+  int out_dtype;
+  int64_t n1, n2;  // out dims 1, 2
+};
+
+__global__ void __launch_bounds__(128) kv4_lse_merge(const LseParams P) {
+  const int64_t r = blockIdx.x;
+  float M = kNegInf;
+  for (int64_t p = 0; p < P.nparts; ++p) M = fmaxf(M, P.pl[p * P.rows + r]);
+  float W = 0.0f;
+  for (int64_t p = 0; p < P.nparts; ++p)
+    W += (M == kNegInf) ? 0.0f : expf(P.pl[p * P.rows + r] - M);
+  const float invW = W > 0.0f ? 1.0f / W : 0.0f;
+  const int64_t i2 = r % P.n2, i01 = r / P.n2, i1 = i01 % P.n1, i0 = i01 / P.n1;
+  for (int dd = threadIdx.x; dd < P.d; dd += blockDim.x) {
+    float o = 0.0f;
+    for (int64_t p = 0; p < P.nparts; ++p) {
+      const float lp = P.pl[p * P.rows + r];
+      const float w = (M == kNegInf) ? 0.0f : expf(lp - M);
+      o += w * P.po[(p * P.rows + r) * P.d + dd];
+    }
+    store_from_f32(P.out, P.out_dtype, i0 * P.os[0] + i1 * P.os[1] + i2 * P.os[2] + dd * P.os[3],
+                   o * invW);
+  }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct Shape {
+  int64_t B, Hq, Hkv, sq, sk, d, pw, ng;
+  int G;
+};
+
+static bool is_float(int dt) { return dt == KV4_F32 || dt == KV4_F16 || dt == KV4_BF16; }
+
+static int validate(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
+                    const kv4_tensor *vp, const kv4_tensor *vs, int G, Shape &S) {
+  if (!q || !kp || !ks || !vp || !vs) return KV4_ERR_INVALID;
+  if (G <= 0) return KV4_ERR_INVALID;
+  if (!is_float(q->dtype) || kp->dtype != KV4_U8 || vp->dtype != KV4_U8 || !is_float(ks->dtype) ||
+      ks->dtype != vs->dtype)
+    return KV4_ERR_DTYPE;
+  for (int i = 0; i < 4; ++i) {
+    if (kp->shape[i] != vp->shape[i] || ks->shape[i] != vs->shape[i]) return KV4_ERR_SHAPE;
+    if (i < 3 && kp->shape[i] != ks->shape[i]) return KV4_ERR_SHAPE;
+  }
+  S.B = q->shape[0];
+  S.Hq = q->shape[1];
+  S.sq = q->shape[2];
+  S.d = q->shape[3];
+  S.Hkv = kp->shape[1];
+  S.sk = kp->shape[2];
+  S.pw = kp->shape[3];
+  S.ng = ks->shape[3];
+  S.G = G;
+  if (kp->shape[0] != S.B) return KV4_ERR_SHAPE;
+  if (S.Hkv <= 0 || S.Hq <= 0 || S.Hq % S.Hkv != 0) return KV4_ERR_INVALID;
+  if (S.pw < (S.d + 1) / 2 || S.ng < (S.d + G - 1) / G) return KV4_ERR_SHAPE;
+  if (S.d > 512) return KV4_ERR_UNSUPPORTED;
+  return KV4_OK;
+}
+
+struct Plan {
+  int path;  // 1 fast, 2 generic
+  int D, sdt;
+  bool split;
+  int hc, ncols, tpu, L, maxp, ctas, units;
+  int64_t total_tiles;
+  size_t ws_bytes;
+  bool need_merge;
+};
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static bool fast_eligible(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
+                          const kv4_tensor *vp, const kv4_tensor *vs, const Shape &S) {
+  if (!(S.d == 64 || S.d == 128 || S.d == 256)) return false;
+  if (!(S.G == 32 || S.G == 64 || S.G == 128) || S.G > S.d || S.d % S.G) return false;
+  if (S.sk <= 0 || S.sk >= (1LL << 31) / 8) return false;
+  const int64_t ng = S.d / S.G;
+  const int ss = dtype_size(ks->dtype);
+  for (const kv4_tensor *t : {kp, vp}) {
+    if (!aligned16(t->data) || t->stride[3] != 1 || t->stride[2] % 16) return false;
+    if (t->shape[1] > 1 && t->stride[1] % 16) return false;
+    if (t->shape[0] > 1 && t->stride[0] % 16) return false;
+  }
+  for (const kv4_tensor *t : {ks, vs}) {
+    if (!aligned16(t->data) || t->stride[3] != 1 || t->shape[3] != ng || t->stride[2] != ng)
+      return false;
+    if (t->shape[1] > 1 && (t->stride[1] * ss) % 16) return false;
+    if (t->shape[0] > 1 && (t->stride[0] * ss) % 16) return false;
+  }
+  if (S.Hq / S.Hkv * S.sq > 8 * NCOL) return false;  // long query blocks: generic
+  (void)q;
+  return get_encode() != nullptr;
+}
+
+template <int D, int G, typename ST, bool SPLIT>
+static int occupancy_of() {
+  static int occ = -1;
+  if (occ < 0) {
+    using Cfg = FastCfg<D, G, ST>;
+    cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT>, 128,
+                                                      Cfg::SMEM) != cudaSuccess ||
+        o < 1)
+      o = 1;
+    occ = o;
+  }
+  return occ;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int D, int G, typename ST, bool SPLIT, typename F>
+static auto with_occ(F &&f) {
+  return f(occupancy_of<D, G, ST, SPLIT>());
+}
+
+static int fast_occupancy(int D, int G, int sdt, bool split) {
+#define KV4_OCC(DD, GG, STT)                                                         \
+  if (D == DD && G == GG) return split ? occupancy_of<DD, GG, STT, true>()           \
+                                       : occupancy_of<DD, GG, STT, false>();
+#define KV4_OCC_S(STT)                                                               \
+  KV4_OCC(64, 32, STT) KV4_OCC(64, 64, STT) KV4_OCC(128, 32, STT) KV4_OCC(128, 64, STT) \
+      KV4_OCC(128, 128, STT) KV4_OCC(256, 32, STT) KV4_OCC(256, 64, STT)              \
+          KV4_OCC(256, 128, STT)
+  if (sdt == KV4_BF16) { KV4_OCC_S(__nv_bfloat16) }
+  else if (sdt == KV4_F16) { KV4_OCC_S(__half) }
+  else { KV4_OCC_S(float) }
+#undef KV4_OCC_S
+#undef KV4_OCC
+  return 1;
+}
+
+static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
+                      const kv4_tensor *vp, const kv4_tensor *vs, const Shape &S,
+                      const kv4_attn_opts *opts, Plan &pl) {
+  pl = Plan{};
+  const bool force_generic = opts && opts->force_generic;
+  if (!force_generic && fast_eligible(q, kp, ks, vp, vs, S)) {
+    pl.path = 1;
+    pl.D = static_cast<int>(S.d);
+    pl.sdt = ks->dtype;
+    pl.split = q->dtype != KV4_BF16;
+    const int R = static_cast<int>(S.Hq / S.Hkv);
+    pl.ncols = R * static_cast<int>(S.sq);
+    pl.hc = (pl.ncols + NCOL - 1) / NCOL;
+    pl.units = static_cast<int>(S.B * S.Hkv * pl.hc);
+    pl.tpu = static_cast<int>((S.sk + TOK - 1) / TOK);
+    pl.total_tiles = static_cast<int64_t>(pl.units) * pl.tpu;
+    const int occ = fast_occupancy(pl.D, S.G, pl.sdt, pl.split);
+    int64_t target = static_cast<int64_t>(sm_count()) * occ;
+    if (opts && opts->max_ctas > 0) target = std::min<int64_t>(target, opts->max_ctas);
+    int64_t L = (pl.total_tiles + target - 1) / target;
+    if (L < 2) L = 2;
+    if (opts && opts->tiles_per_cta > 0) L = opts->tiles_per_cta;
+    pl.L = static_cast<int>(L);
+    pl.ctas = static_cast<int>((pl.total_tiles + L - 1) / L);
+    pl.maxp = static_cast<int>((pl.tpu - 1 + L - 1) / L + 1);
+    pl.need_merge = (L % pl.tpu) != 0;
+    pl.ws_bytes = pl.need_merge ? static_cast<size_t>(pl.units) * pl.maxp * NCOL *
+                                      (static_cast<size_t>(pl.D) + 1) * sizeof(float)
+                                : 0;
+  } else {
+    pl.path = 2;
+    pl.ws_bytes = 0;
+    pl.ctas = static_cast<int>(S.B * S.Hq * S.sq);
+    pl.need_merge = false;
+  }
+}
+
+static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int box_inner, int swz_bytes) {
+  auto enc = get_encode();
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t->shape[3]), static_cast<cuuint64_t>(t->shape[2]),
+                        static_cast<cuuint64_t>(t->shape[1]),
+                        static_cast<cuuint64_t>(t->shape[0])};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t->stride[2]),
+                           static_cast<cuuint64_t>(t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2]),
+                           static_cast<cuuint64_t>(t->shape[0] > 1 ? t->stride[0] : (t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2]) * t->shape[1])};
+  // strides must be multiples of 16 even for size-1 dims; round the synthetic ones up
+  for (int i = 0; i < 3; ++i) strides[i] = (strides[i] + 15) / 16 * 16;
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(TOK), 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUtensorMapSwizzle sw = swz_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                          : swz_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, t->data, dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
+}
+
+static int encode_scales(CUtensorMap *tm, const kv4_tensor *t, int tokens_per_box) {
+  auto enc = get_encode();
+  const int ss = dtype_size(t->dtype);
+  const int64_t ng = t->shape[3];
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(t->shape[2] * ng),
+                        static_cast<cuuint64_t>(t->shape[1]),
+                        static_cast<cuuint64_t>(t->shape[0])};
+  int64_t s1 = t->shape[1] > 1 ? t->stride[1] : t->shape[2] * ng;
+  int64_t s0 = t->shape[0] > 1 ? t->stride[0] : s1 * t->shape[1];
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>((s1 * ss + 15) / 16 * 16),
+                           static_cast<cuuint64_t>((s0 * ss + 15) / 16 * 16)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(tokens_per_box * ng), 1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUtensorMapDataType dt =
+      ss == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUresult r = enc(tm, dt, 3, t->data, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
+}
+
+template <int D, int G, typename ST, bool SPLIT>
+static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
+                         const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
+                         cudaStream_t st) {
+  using Cfg = FastCfg<D, G, ST>;
+  CUtensorMap tkp, tvp, tks, tvs;
+  int rc;
+  if ((rc = encode_packed(&tkp, kp, Cfg::P, Cfg::P))) return rc;
+  if ((rc = encode_packed(&tvp, vp, Cfg::P, Cfg::P))) return rc;
+  if ((rc = encode_scales(&tks, ks, Cfg::TS))) return rc;
+  if ((rc = encode_scales(&tvs, vs, Cfg::TS))) return rc;
+  occupancy_of<D, G, ST, SPLIT>();  // sets the smem attribute once
+  kv4_attn_fast<D, G, ST, SPLIT><<<pl.ctas, 128, Cfg::SMEM, st>>>(FP, tkp, tvp, tks, tvs);
+  rc = cuda_status(cudaGetLastError());
+  if (rc) return rc;
+  if (pl.need_merge) {
+    dim3 grid(pl.units, NCOL);
+    kv4_merge_slots<<<grid, 128, 0, st>>>(FP);
+    rc = cuda_status(cudaGetLastError());
+  }
+  return rc;
+}
+
+template <int D, int G, typename ST>
+static int launch_fast_s(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
+                         const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
+                         cudaStream_t st) {
+  return pl.split ? launch_fast_t<D, G, ST, true>(FP, pl, kp, ks, vp, vs, st)
+                  : launch_fast_t<D, G, ST, false>(FP, pl, kp, ks, vp, vs, st);
+}
+
+template <typename ST>
+static int launch_fast_st(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
+                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
+                          cudaStream_t st) {
+  const int D = pl.D, G = FP.c.G;
+#define KV4_L(DD, GG) \
+  if (D == DD && G == GG) return launch_fast_s<DD, GG, ST>(FP, pl, kp, ks, vp, vs, st);
+  KV4_L(64, 32) KV4_L(64, 64) KV4_L(128, 32) KV4_L(128, 64) KV4_L(128, 128) KV4_L(256, 32)
+      KV4_L(256, 64) KV4_L(256, 128)
+#undef KV4_L
+  return KV4_ERR_UNSUPPORTED;
+}
+
+static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
+                         const kv4_tensor *vp, const kv4_tensor *vs, const kv4_tensor *out,
+                         const kv4_tensor *lse, int mode, int64_t k_offset, int64_t sk_total,
+                         int G, int is_causal, float sm_scale, void *ws, size_t ws_bytes,
+                         const kv4_attn_opts *opts, cudaStream_t st) {
+  Shape S;
+  int rc = validate(q, kp, ks, vp, vs, G, S);
+  if (rc) return rc;
+  if (!out) return KV4_ERR_INVALID;
+  for (int i = 0; i < 4; ++i)
+    if (out->shape[i] != q->shape[i]) return KV4_ERR_SHAPE;
+  if (mode == OUT_FINAL) {
+    if (out->dtype != q->dtype) return KV4_ERR_DTYPE;
+  } else {
+    if (out->dtype != KV4_F32 || !lse || lse->dtype != KV4_F32) return KV4_ERR_DTYPE;
+    for (int i = 0; i < 3; ++i)
+      if (lse->shape[i] != q->shape[i]) return KV4_ERR_SHAPE;
+  }
+  if (S.B == 0 || S.Hq == 0 || S.sq == 0 || S.d == 0) return KV4_OK;
+
+  AttnCommon Cm{};
+  Cm.q = q->data;
+  Cm.q_dtype = q->dtype;
+  Cm.out = out->data;
+  Cm.out_dtype = out->dtype;
+  for (int i = 0; i < 4; ++i) {
+    Cm.qs[i] = q->stride[i];
+    Cm.os[i] = out->stride[i];
+  }
+  if (lse) {
+    Cm.lse = static_cast<float *>(lse->data);
+    for (int i = 0; i < 3; ++i) Cm.ls[i] = lse->stride[i];
+  }
+  Cm.mode = mode;
+  Cm.B = static_cast<int>(S.B);
+  Cm.Hq = static_cast<int>(S.Hq);
+  Cm.Hkv = static_cast<int>(S.Hkv);
+  Cm.R = static_cast<int>(S.Hq / S.Hkv);
+  Cm.sq = static_cast<int>(S.sq);
+  Cm.sk = static_cast<int>(S.sk);
+  Cm.d = static_cast<int>(S.d);
+  Cm.G = G;
+  Cm.causal = is_causal ? 1 : 0;
+  Cm.k_offset = mode == OUT_PARTIAL ? k_offset : 0;
+  Cm.sk_total = mode == OUT_PARTIAL ? sk_total : S.sk;
+  const float sc = sm_scale > 0.0f ? sm_scale : 1.0f / sqrtf(static_cast<float>(S.d));
+  Cm.scale_log2 = sc * kLog2e;
+
+  Plan pl;
+  make_plan(q, kp, ks, vp, vs, S, opts, pl);
+  if (pl.path == 1) {
+    if (pl.ws_bytes > 0 && (ws == nullptr || ws_bytes < pl.ws_bytes)) return KV4_ERR_WORKSPACE;
+    FastParams FP{};
+    FP.c = Cm;
+    FP.ncols = pl.ncols;
+    FP.hc = pl.hc;
+    FP.tpu = pl.tpu;
+    FP.L = pl.L;
+    FP.total_tiles = pl.total_tiles;
+    FP.maxp = pl.maxp;
+    FP.ws_o = static_cast<float *>(ws);
+    FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) * pl.maxp * NCOL * pl.D
+                            : nullptr;
+    if (pl.sdt == KV4_BF16) return launch_fast_st<__nv_bfloat16>(FP, pl, kp, ks, vp, vs, st);
+    if (pl.sdt == KV4_F16) return launch_fast_st<__half>(FP, pl, kp, ks, vp, vs, st);
+    return launch_fast_st<float>(FP, pl, kp, ks, vp, vs, st);
+  }
+  // generic
+  GenParams GP{};
+  GP.c = Cm;
+  GP.kp = static_cast<const uint8_t *>(kp->data);
+  GP.vp = static_cast<const uint8_t *>(vp->data);
+  GP.ks = ks->data;
+  GP.vs = vs->data;
+  for (int i = 0; i < 4; ++i) {
+    GP.kps[i] = kp->stride[i];
+    GP.vps[i] = vp->stride[i];
+    GP.kss[i] = ks->stride[i];
+    GP.vss[i] = vs->stride[i];
+  }
+  GP.s_dtype = ks->dtype;
+  dim3 grid(static_cast<unsigned>(S.B * S.Hq), static_cast<unsigned>(S.sq));
+  if (S.d <= 64) kv4_attn_generic<2><<<grid, 128, 0, st>>>(GP);
+  else if (S.d <= 128) kv4_attn_generic<4><<<grid, 128, 0, st>>>(GP);
+  else if (S.d <= 256) kv4_attn_generic<8><<<grid, 128, 0, st>>>(GP);
+  else kv4_attn_generic<16><<<grid, 128, 0, st>>>(GP);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace kv4
+
+using namespace kv4;
+
+extern "C" int kv4_attention(const kv4_tensor *q, const kv4_tensor *k_packed,
+                             const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                             const kv4_tensor *v_scales, const kv4_tensor *out, int group_size,
+                             int is_causal, float sm_scale, void *workspace,
+                             size_t workspace_bytes, const kv4_attn_opts *opts, void *stream) {
+  return run_attention(q, k_packed, k_scales, v_packed, v_scales, out, nullptr, OUT_FINAL, 0, 0,
+                       group_size, is_causal, sm_scale, workspace, workspace_bytes, opts,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kv4_attention_partial(const kv4_tensor *q, const kv4_tensor *k_packed,
+                                     const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                                     const kv4_tensor *v_scales, const kv4_tensor *part_o,
+                                     const kv4_tensor *part_lse, int64_t k_offset,
+                                     int64_t sk_total, int group_size, int is_causal,
+                                     float sm_scale, void *workspace, size_t workspace_bytes,
+                                     const kv4_attn_opts *opts, void *stream) {
+  if (k_offset < 0 || sk_total < k_offset + (k_packed ? k_packed->shape[2] : 0))
+    return KV4_ERR_INVALID;
+  return run_attention(q, k_packed, k_scales, v_packed, v_scales, part_o, part_lse, OUT_PARTIAL,
+                       k_offset, sk_total, group_size, is_causal, sm_scale, workspace,
+                       workspace_bytes, opts, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kv4_attention_plan(const kv4_tensor *q, const kv4_tensor *k_packed,
+                                  const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                                  const kv4_tensor *v_scales, const kv4_tensor *out,
+                                  int group_size, int is_causal, const kv4_attn_opts *opts,
+                                  kv4_attn_plan *plan) {
+  (void)out;
+  (void)is_causal;
+  if (!plan) return KV4_ERR_INVALID;
+  Shape S;
+  int rc = validate(q, k_packed, k_scales, v_packed, v_scales, group_size, S);
+  if (rc) return rc;
+  Plan pl;
+  make_plan(q, k_packed, k_scales, v_packed, v_scales, S, opts, pl);
+  plan->path = pl.path;
+  plan->ctas = pl.ctas;
+  plan->tiles_per_cta = pl.L;
+  plan->units = pl.units;
+  plan->max_parts = pl.maxp;
+  plan->kernels = pl.need_merge ? 2 : 1;
+  plan->workspace_bytes = static_cast<int64_t>(pl.ws_bytes);
+  return KV4_OK;
+}
+
+extern "C" int kv4_lse_combine(const float *parts_o, const float *parts_lse, int64_t n_parts,
+                               const kv4_tensor *out, void *stream) {
+  if (!parts_o || !parts_lse || !out || n_parts <= 0) return KV4_ERR_INVALID;
+  if (!is_float(out->dtype)) return KV4_ERR_DTYPE;
+  const int64_t rows = out->shape[0] * out->shape[1] * out->shape[2];
+  if (rows == 0 || out->shape[3] == 0) return KV4_OK;
+  if (rows > 0x7fffffff) return KV4_ERR_UNSUPPORTED;
+  LseParams P{};
+  P.po = parts_o;
+  P.pl = parts_lse;
+  P.nparts = n_parts;
+  P.rows = rows;
+  P.d = static_cast<int>(out->shape[3]);
+  P.out = out->data;
+  for (int i = 0; i < 4; ++i) P.os[i] = out->stride[i];
+  P.out_dtype = out->dtype;
+  P.n1 = out->shape[1];
+  P.n2 = out->shape[2];
+  kv4_lse_merge<<<static_cast<unsigned>(rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(P);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int kv4_device_error(void *stream, int *flag_out) {
+  if (!flag_out) return KV4_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = cuda_status(cudaStreamSynchronize(st));
+  if (rc) return rc;
+  int v = 0, zero = 0;
+  rc = cuda_status(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  if (rc) return rc;
+  rc = cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  *flag_out = v;
+  return rc;
+}

@@ -1,0 +1,3 @@
+"""GPT-2 INT4 KV-cache kernels (sm_100a CUDA via libkvint4.so)."""
+
+__all__ = []

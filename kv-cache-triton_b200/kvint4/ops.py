@@ -1,0 +1,163 @@
+"""Thin torch-facing wrappers over the C ABI (pointers, strides, current stream).
+
+These functions do no validation beyond what is needed to build the
+descriptors; the reference-shaped public functions in ``kernels.*`` perform
+the reference's checks (and raise its ``ValueError`` messages) first.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import AttnOpts, AttnPlan, Tensor, check, lib
+
+_DT = {torch.float32: _lib.KV4_F32, torch.float16: _lib.KV4_F16,
+       torch.bfloat16: _lib.KV4_BF16, torch.uint8: _lib.KV4_U8}
+
+
+def desc(t: torch.Tensor) -> Tensor:
+    """kv4_tensor for ``t`` (rank <= 4, leading dims padded with size 1)."""
+    n = t.dim()
+    if not 1 <= n <= 4:
+        raise ValueError("kvint4 tensors have 1 to 4 dims")
+    shape = [1] * (4 - n) + list(t.shape)
+    stride = [0] * (4 - n) + list(t.stride())
+    for i in range(3 - n, -1, -1):  # padded size-1 dims get the natural stride
+        stride[i] = stride[i + 1] * shape[i + 1]
+    d = Tensor()
+    d.data = t.data_ptr()
+    d.dtype = _DT[t.dtype]
+    for i in range(4):
+        d.shape[i] = int(shape[i])
+        d.stride[i] = int(stride[i])
+    return d
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, group_size: int,
+                  tie: int = _lib.TIE_HALF_AWAY, t_off: int = 0) -> None:
+    L = lib()
+    dx, dp, ds = desc(x), desc(packed), desc(scales)
+    check("kv4_quantize", L.kv4_quantize(ctypes.byref(dx), ctypes.byref(dp), ctypes.byref(ds),
+                                         int(t_off), int(group_size), int(tie), _stream(x.device)))
+
+
+def append_kv(k, v, k_packed, k_scales, v_packed, v_scales, pos: int, group_size: int,
+              tie: int = _lib.TIE_HALF_AWAY) -> None:
+    L = lib()
+    ds = [desc(t) for t in (k, v, k_packed, k_scales, v_packed, v_scales)]
+    check("kv4_append_kv", L.kv4_append_kv(*[ctypes.byref(d) for d in ds], int(pos),
+                                           int(group_size), int(tie), _stream(k.device)))
+
+
+def dequantize_into(packed: torch.Tensor, scales: torch.Tensor, out: torch.Tensor,
+                    group_size: int) -> None:
+    L = lib()
+    dp, ds, do = desc(packed), desc(scales), desc(out)
+    check("kv4_dequantize", L.kv4_dequantize(ctypes.byref(dp), ctypes.byref(ds),
+                                             ctypes.byref(do), int(group_size),
+                                             _stream(packed.device)))
+
+
+# --------------------------------------------------------------------------
+# attention
+# --------------------------------------------------------------------------
+_WS: dict = {}
+
+
+def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Per (device, stream) scratch buffer for split-sequence partials."""
+    if nbytes <= 0:
+        return None
+    key = (dev.index, _stream(dev))
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0):
+    if not (force_generic or tiles_per_cta or max_ctas):
+        return None
+    o = AttnOpts()
+    o.force_generic = int(bool(force_generic))
+    o.tiles_per_cta = int(tiles_per_cta)
+    o.max_ctas = int(max_ctas)
+    return o
+
+
+def plan(q, kp, ks, vp, vs, out, group_size, is_causal=False, **kw) -> AttnPlan:
+    L = lib()
+    ds = [desc(t) for t in (q, kp, ks, vp, vs, out)]
+    o = _opts(**kw)
+    p = AttnPlan()
+    check("kv4_attention_plan",
+          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
+                               ctypes.byref(o) if o else None, ctypes.byref(p)))
+    return p
+
+
+def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = False,
+                   sm_scale: float = 0.0, **kw) -> None:
+    L = lib()
+    ds = [desc(t) for t in (q, kp, ks, vp, vs, out)]
+    o = _opts(**kw)
+    optr = ctypes.byref(o) if o else None
+    p = AttnPlan()
+    check("kv4_attention_plan",
+          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
+                               optr, ctypes.byref(p)))
+    ws = _workspace(q.device, int(p.workspace_bytes))
+    check("kv4_attention",
+          L.kv4_attention(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
+                          float(sm_scale), ws.data_ptr() if ws is not None else None,
+                          ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+
+
+def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, sk_total: int,
+                           group_size: int, is_causal: bool = False, sm_scale: float = 0.0,
+                           **kw) -> None:
+    L = lib()
+    ds = [desc(t) for t in (q, kp, ks, vp, vs, part_o)]
+    dl = desc(part_lse)
+    o = _opts(**kw)
+    optr = ctypes.byref(o) if o else None
+    p = AttnPlan()
+    check("kv4_attention_plan",
+          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
+                               optr, ctypes.byref(p)))
+    ws = _workspace(q.device, int(p.workspace_bytes))
+    check("kv4_attention_partial",
+          L.kv4_attention_partial(*[ctypes.byref(d) for d in ds], ctypes.byref(dl),
+                                  int(k_offset), int(sk_total), int(group_size), int(is_causal),
+                                  float(sm_scale), ws.data_ptr() if ws is not None else None,
+                                  ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+
+
+def lse_combine_into(parts_o: torch.Tensor, parts_lse: torch.Tensor, out: torch.Tensor) -> None:
+    """parts_o f32 [P, rows, d] contiguous, parts_lse f32 [P, rows] contiguous."""
+    L = lib()
+    if not (parts_o.is_contiguous() and parts_lse.is_contiguous()):
+        raise ValueError("parts must be contiguous")
+    if parts_o.dtype != torch.float32 or parts_lse.dtype != torch.float32:
+        raise ValueError("parts must be float32")
+    do = desc(out)
+    check("kv4_lse_combine", L.kv4_lse_combine(parts_o.data_ptr(), parts_lse.data_ptr(),
+                                               int(parts_o.shape[0]), ctypes.byref(do),
+                                               _stream(out.device)))
+
+
+def device_error(dev: torch.device | None = None) -> int:
+    """Read and clear the device error word set by bounded waits."""
+    L = lib()
+    flag = ctypes.c_int(0)
+    dev = dev or torch.device("cuda", torch.cuda.current_device())
+    check("kv4_device_error", L.kv4_device_error(_stream(dev), ctypes.byref(flag)))
+    return flag.value

@@ -1,0 +1,87 @@
+"""Quantized KV cache for GPT-2 decode with packed INT4 storage.
+
+Drop-in for the reference's ``models/gpt2/kv_cache.py`` (``QuantizedKVCache``
+:21-112): scales are always fp16 and dequantization returns fp16;
+``get_max_cache_shape()`` takes no layer argument and returns ``None``.
+Storage and append are the in-place capacity buffers of ``kvint4.cache``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from kvint4._lib import TIE_HALF_AWAY
+from kvint4.cache import Int4KVStore
+
+
+class QuantizedKVCache:
+    """Minimal cache object compatible with GPT-2 cache usage."""
+
+    def __init__(self, group_size: int = 32, *, capacity: int | None = None,
+                 tie_mode: int = TIE_HALF_AWAY):
+        if group_size <= 0:
+            raise ValueError("group_size must be > 0")
+        self.group_size = int(group_size)
+        self._store = Int4KVStore(self.group_size, capacity=capacity,
+                                  scale_dtype=torch.float16, tie_mode=tie_mode)
+
+    @property
+    def _layers(self):
+        return self._store._layers
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        layer = self._layers.get(layer_idx)
+        return 0 if layer is None else int(layer.seq_len)
+
+    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int = 0) -> tuple[int, int]:
+        past_len = self.get_seq_length(layer_idx)
+        if isinstance(cache_position, torch.Tensor):
+            query_length = int(cache_position.shape[0]) if cache_position.dim() else int(
+                cache_position.item())
+        else:
+            query_length = int(cache_position)
+        return past_len + query_length, 0
+
+    def get_max_cache_shape(self) -> int | None:
+        return None
+
+    @property
+    def is_initialized(self) -> bool:
+        return len(self._layers) > 0
+
+    @property
+    def is_sliding(self) -> list[bool]:
+        return [False for _ in self._layers]
+
+    def __len__(self) -> int:
+        return len(self._layers)
+
+    def reset(self) -> None:
+        self._layers.clear()
+
+    def has_layer(self, layer_idx: int) -> bool:
+        return layer_idx in self._layers
+
+    def append(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int) -> None:
+        self._store.append(key_states, value_states, layer_idx)
+
+    def update(
+        self,
+        key_states: torch.Tensor,
+        value_states: torch.Tensor,
+        layer_idx: int,
+        cache_kwargs: dict | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """Quantize and append K/V, then return dequantized full cache for compatibility."""
+        del cache_kwargs
+        self._store.append(key_states, value_states, layer_idx)
+        return self.get_dequantized(layer_idx)
+
+    def get_quantized(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        return self._store.layer(layer_idx).views()
+
+    def get_dequantized(self, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return self._store.dequantized(layer_idx, torch.float16)
+
+    def nbytes(self) -> int:
+        return self._store.nbytes()

@@ -1,0 +1,187 @@
+"""Fused INT4 attention on the GPU vs the CPU oracle (float64 attention over the
+same dequantized cache).  Tolerances (max-abs): fp32 1e-3, fp16 5e-3,
+bf16 2e-2 -- the bounds the north star states for fp32 and bf16."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import cases, load, to_f32
+from helpers import ATOL, f32, kv_inputs, oracle_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(b, hq, hkv, sq, sk, d, gs, qdt, causal=False, seed=0, sdt=None, **kw):
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    from kernels.llama3.quantize import quantize_int4
+    from kvint4 import frontend
+    k, v = kv_inputs(b, hkv, sk, d, dtype=qdt, seed=seed, device="cuda")
+    g = torch.Generator().manual_seed(seed + 100)
+    q = torch.randn(b, hq, sq, d, generator=g).to(qdt).cuda()
+    kp, ks = quantize_int4(k, gs)
+    vp, vs = quantize_int4(v, gs)
+    if sdt is not None:
+        ks, vs = ks.to(sdt), vs.to(sdt)
+    if kw:
+        out = frontend.attention(q, kp, ks, vp, vs, n_q_heads=hq, n_kv_heads=hkv,
+                                 group_size=gs, is_causal=causal, **kw)
+    else:
+        out = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=hq, n_kv_heads=hkv,
+                                          group_size=gs, is_causal=causal)
+    ref = oracle_attention(q, kp, ks, vp, vs, n_q_heads=hq, n_kv_heads=hkv, group_size=gs,
+                           is_causal=causal)
+    return q, (kp, ks, vp, vs), out, ref
+
+
+def _plan_path(q, cache, gs, causal=False, **kw):
+    from kvint4 import ops
+    out = torch.empty_like(q)
+    return ops.plan(q, *cache, out, gs, causal, **kw).path
+
+
+@pytest.mark.parametrize("qdt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("d,gs", [(128, 32), (128, 64), (128, 128), (64, 32), (64, 64),
+                                  (256, 32), (256, 128)])
+def test_decode_fast_path_matches_oracle(qdt, d, gs):
+    q, cache, out, ref = _run(2, 8, 2, 1, 301, d, gs, qdt)
+    assert _plan_path(q, cache, gs) == 1
+    assert out.dtype == qdt and torch.isfinite(out).all()
+    np.testing.assert_allclose(f32(out), ref, atol=ATOL[qdt], rtol=0)
+
+
+@pytest.mark.parametrize("ratio", [1, 2, 4, 8, 16])
+def test_decode_gqa_ratios(ratio):
+    q, cache, out, ref = _run(2, 2 * ratio, 2, 1, 200, 128, 32, torch.bfloat16)
+    np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("sk", [1, 2, 15, 63, 64, 65, 127, 129, 1000, 4099])
+def test_decode_ragged_lengths(sk):
+    q, cache, out, ref = _run(3, 8, 2, 1, sk, 128, 32, torch.float32, seed=sk)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize("tiles_per_cta", [1, 2, 3, 5, 7, 64])
+def test_stream_k_split_invariance(tiles_per_cta):
+    """Every split of the sequence across CTAs gives the oracle's answer."""
+    q, cache, out, ref = _run(2, 8, 2, 1, 1000, 128, 32, torch.float32, seed=3,
+                              tiles_per_cta=tiles_per_cta)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize("sq,causal", [(2, True), (3, False), (5, True), (16, True)])
+def test_multi_query_rows_causal_bottom_right(sq, causal):
+    q, cache, out, ref = _run(1, 8, 2, sq, 90, 128, 32, torch.float32, causal=causal, seed=sq)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+def test_generic_path_matches_oracle():
+    q, cache, out, ref = _run(2, 8, 2, 1, 333, 128, 32, torch.float32, force_generic=True)
+    assert _plan_path(q, cache, 32, force_generic=True) == 2
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+    # odd head dim and group size only the generic kernel takes
+    q, cache, out, ref = _run(1, 4, 2, 1, 50, 80, 16, torch.float32)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize("sdt", [torch.float16, torch.float32])
+def test_scale_dtypes(sdt):
+    q, cache, out, ref = _run(2, 8, 2, 1, 257, 128, 32, torch.float32, sdt=sdt)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+def test_cache_views_read_in_place_and_odd_lengths():
+    """The capacity-buffer views (token stride = row, plane stride = capacity)
+    go through the TMA path without copies."""
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    from models.llama3.kv_cache import QuantizedKVCache
+    k, v = kv_inputs(2, 2, 77, 128, device="cuda", seed=9)
+    cache = QuantizedKVCache(group_size=32, capacity=256)
+    cache.append(k, v, 0)
+    kp, ks, vp, vs = cache.get_quantized(0)
+    assert not kp.is_contiguous()
+    q = torch.randn(2, 8, 1, 128, device="cuda").to(torch.bfloat16)
+    assert _plan_path(q, (kp, ks, vp, vs), 32) == 1
+    out = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=8, n_kv_heads=2)
+    ref = oracle_attention(q, kp, ks, vp, vs, n_q_heads=8, n_kv_heads=2, group_size=32)
+    np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
+
+
+def test_config2_shape_full_size_properties():
+    """BASELINE config 2 shape (B16, 32/8 heads, S 4096, d 128, G 32): output
+    against the oracle on a batch slice, split invariance, determinism."""
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    from kernels.llama3.quantize import quantize_int4
+    from kvint4 import frontend
+    k, v = kv_inputs(16, 8, 4096, 128, device="cuda", seed=0)
+    q = torch.randn(16, 32, 1, 128, device="cuda").to(torch.bfloat16)
+    kp, ks = quantize_int4(k, 32)
+    vp, vs = quantize_int4(v, 32)
+    out = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=32, n_kv_heads=8)
+    out2 = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=32, n_kv_heads=8)
+    assert torch.equal(out, out2)  # deterministic
+    one = frontend.attention(q, kp, ks, vp, vs, n_q_heads=32, n_kv_heads=8, group_size=32,
+                             is_causal=False, tiles_per_cta=64)  # one CTA per unit
+    assert (out.float() - one.float()).abs().max().item() <= 2e-2
+    sl = slice(0, 2)
+    ref = oracle_attention(q[sl], kp[sl], ks[sl], vp[sl], vs[sl], n_q_heads=32, n_kv_heads=8,
+                           group_size=32)
+    np.testing.assert_allclose(f32(out[sl]), ref, atol=2e-2, rtol=0)
+
+
+A = load("attn_cases.npz")
+
+
+@pytest.mark.parametrize("case", cases(A))
+def test_attention_golden_reference_cases(case):
+    """The reference's own GQA reference (looped fp32 / SDPA) on the golden inputs."""
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    b, hq, hkv, sq, sk, d, gs, causal = (int(x) for x in A[case + ".meta"])
+    qdt = str(A[case + ".q_dtype"])
+    sdt = str(A[case + ".scale_dtype"])
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+    q = torch.from_numpy(to_f32(A[case + ".q"], qdt)).to(tdt[qdt]).cuda()
+    ks = torch.from_numpy(to_f32(A[case + ".k_scales"], sdt)).to(tdt[sdt]).cuda()
+    vs = torch.from_numpy(to_f32(A[case + ".v_scales"], sdt)).to(tdt[sdt]).cuda()
+    kp = torch.from_numpy(A[case + ".k_packed"]).cuda()
+    vp = torch.from_numpy(A[case + ".v_packed"]).cuda()
+    out = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=hq, n_kv_heads=hkv,
+                                      group_size=gs, is_causal=bool(causal))
+    np.testing.assert_allclose(f32(out), A[case + ".out_ref_f32"], atol=ATOL[tdt[qdt]], rtol=0)
+
+
+def test_partial_and_lse_combine_equal_full():
+    """Sequence shards (kv4_attention_partial) merged by kv4_lse_combine equal
+    the unsharded result -- the math of the multi-GPU sequence-shard layer."""
+    from kernels.llama3.quantize import quantize_int4
+    from kvint4 import ops
+    k, v = kv_inputs(2, 2, 700, 128, dtype=torch.float32, device="cuda", seed=4)
+    q = torch.randn(2, 8, 3, 128, device="cuda")
+    kp, ks = quantize_int4(k, 32)
+    vp, vs = quantize_int4(v, 32)
+    ref = oracle_attention(q, kp, ks, vp, vs, n_q_heads=8, n_kv_heads=2, group_size=32,
+                           is_causal=True)
+    bounds = [0, 150, 301, 650, 700]
+    po = torch.empty(4, 2, 8, 3, 128, device="cuda")
+    pl = torch.empty(4, 2, 8, 3, device="cuda")
+    for r in range(4):
+        a, e = bounds[r], bounds[r + 1]
+        ops.attention_partial_into(q, kp[:, :, a:e], ks[:, :, a:e], vp[:, :, a:e],
+                                   vs[:, :, a:e], po[r], pl[r], a, 700, 32, True)
+    out = torch.empty(2, 8, 3, 128, device="cuda")
+    ops.lse_combine_into(po.reshape(4, -1, 128), pl.reshape(4, -1), out)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+def test_prefill_long_block_routes_and_matches():
+    q, cache, out, ref = _run(1, 4, 2, 300, 300, 128, 32, torch.bfloat16, causal=True)
+    np.testing.assert_allclose(f32(out), ref, atol=3e-2, rtol=0)
+
+
+def test_no_device_error_flag_after_runs():
+    from kvint4 import ops
+    _run(2, 8, 2, 1, 500, 128, 32, torch.bfloat16)
+    assert ops.device_error() == 0
