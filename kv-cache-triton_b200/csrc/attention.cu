@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -175,8 +176,9 @@ __global__ void __launch_bounds__(128) kv4_attn_generic(const GenParams P) {
 // ===========================================================================
 // fast path
 // ===========================================================================
-constexpr int TOK = 64;    // tokens per pipeline stage (4 warps x 16 rows)
+constexpr int TOK = 128;   // tokens per pipeline stage (4 warps x 32 rows)
 constexpr int NWARP = 4;
+constexpr int WROWS = 32;  // token rows per warp per stage (two m16 sub-tiles)
 constexpr int NCOL = 8;    // (head, query row) columns per CTA = MMA N
 
 struct FastParams {
@@ -191,6 +193,10 @@ struct FastParams {
   float *ws_lse;  // [units*maxp][NCOL]   (log2 domain)
 };
 
+// Shared-memory layout of one stage (per tensor): packed codes chunk-major,
+// [chunk (16 B = 32 dims)][token][16 B], so that every fragment load is a
+// lane-constant base plus an immediate and all accesses are bank-conflict
+// free; scales token-major [token][group].
 template <int D, int G, typename ST>
 struct FastCfg {
   static constexpr int P = D / 2;             // packed bytes per token
@@ -198,30 +204,38 @@ struct FastCfg {
   static constexpr int NG = D / G;            // scale groups per token
   static constexpr int CPG = G / 32;          // chunks per group
   static constexpr int SROW = NG * (int)sizeof(ST);  // scale bytes per token
+  static constexpr int CH = TOK * 16;         // bytes of one chunk plane
   static constexpr int KP = TOK * P;          // packed bytes per stage per tensor
   static constexpr int KS = TOK * SROW;       // scale bytes per stage per tensor
   static constexpr int TS = (TOK * NG <= 256) ? TOK : 256 / NG;  // tokens per scale TMA box
   static constexpr int NSB = TOK / TS;        // scale boxes per stage per tensor
   static constexpr int STAGE = ((2 * KP + 2 * KS) + 1023) / 1024 * 1024;
-  static constexpr int STAGES = (D == 256) ? 3 : 4;
-  static constexpr int SWZ = (P == 32) ? 1 : (P == 64) ? 3 : 7;
+  static constexpr int STAGES = (D == 256) ? 2 : 3;
   static constexpr int MERGE = NWARP * NCOL * D * 4;
   static constexpr int SMEM = STAGES * STAGE + MERGE + 2 * NWARP * NCOL * 4 + 64 + 1024;
   static constexpr uint32_t TX = 2 * KP + 2 * KS;
 };
 
-// physical byte offset of logical offset o in a TMA-swizzled [TOK][P] tile
-template <int SWZ>
-__device__ __forceinline__ uint32_t swz(uint32_t o) {
-  return o ^ (((o >> 7) & SWZ) << 4);
+// Nibble extraction into bf16x2 "128 + code" values (exact; bf16 0x4300|n ==
+// 128 + n).  Each picks the same nibble of bytes k and k+2 of x into the low
+// and high 16-bit halves.  Only the byte-0/2 low nibbles sit in place; the
+// others are moved with mad.hi (x & mask) * 2^s + magic, which runs on the
+// FMA pipe instead of the half-rate integer ALU pipe a shift would use.
+__device__ __forceinline__ uint32_t madhi(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
 }
-
-// nibble extraction into bf16x2 "128 + code" values (exact): low nibbles of
-// bytes 0 and 2 of x land in the low and high halves.
-__device__ __forceinline__ uint32_t nib2(uint32_t x) { return (x & 0x000F000Fu) | 0x43004300u; }
-
-template <typename ST>
-__device__ __forceinline__ void load_scales(uint32_t addr, float (&s)[8], int ng);
+__device__ __forceinline__ uint32_t nib_lo0(uint32_t x) { return (x & 0x000F000Fu) | 0x43004300u; }
+__device__ __forceinline__ uint32_t nib_hi0(uint32_t x) {
+  return madhi(x & 0x00F000F0u, 1u << 28, 0x43004300u);
+}
+__device__ __forceinline__ uint32_t nib_lo1(uint32_t x) {
+  return madhi(x & 0x0F000F00u, 1u << 24, 0x43004300u);
+}
+__device__ __forceinline__ uint32_t nib_hi1(uint32_t x) {
+  return madhi(x & 0xF000F000u, 1u << 20, 0x43004300u);
+}
 
 template <int NG, typename ST>
 __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
@@ -265,7 +279,7 @@ __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
 }
 
 template <int D, int G, typename ST, bool SPLIT>
-__global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
+__global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
                   const __grid_constant__ CUtensorMap tm_vp,
                   const __grid_constant__ CUtensorMap tm_ks,
@@ -287,9 +301,9 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
   const int lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tg = lane & 3;
 
-  const int64_t first_tile = static_cast<int64_t>(blockIdx.x) * P.L;
-  const int64_t last_tile = min(first_tile + P.L, P.total_tiles);  // exclusive
-  const int ntiles = static_cast<int>(last_tile - first_tile);
+  const int first_tile = static_cast<int>(blockIdx.x) * P.L;  // total tiles < 2^31 (host check)
+  const int last_tile = min(first_tile + P.L, static_cast<int>(P.total_tiles));  // exclusive
+  const int ntiles = last_tile - first_tile;
   if (ntiles <= 0) return;
 
   const uint32_t smem_base = smem_u32(smem);
@@ -306,22 +320,32 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
   }
   __syncthreads();
 
-  // unit -> (b, kvh, column chunk)
-  auto unit_of = [&](int64_t gt) { return static_cast<int>(gt / P.tpu); };
+  // Tile bookkeeping is incremental: the (unit, tile-in-unit) of the first
+  // tile costs one division; afterwards both the consumer position and the
+  // producer's (STAGES ahead) advance by +1 with a wrap at tpu.
+  const int u_first = first_tile / P.tpu;
+  const int ti_first = first_tile - u_first * P.tpu;
+  int iss_u = u_first, iss_ti = ti_first, iss_b = 0, iss_kvh = 0, iss_bu = -1;
 
-  auto issue = [&](int i) {  // local tile i -> stage i % STAGES
-    const int64_t gt = first_tile + i;
-    const int u = unit_of(gt);
-    const int ti = static_cast<int>(gt - static_cast<int64_t>(u) * P.tpu);
-    const int bk = u / P.hc;
-    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
-    const int t0 = ti * TOK;
+  auto issue = [&](int i) {  // next tile in order -> stage i % STAGES (thread 0 only)
+    if (iss_u != iss_bu) {
+      const int bk = iss_u / P.hc;
+      iss_b = bk / C.Hkv;
+      iss_kvh = bk - iss_b * C.Hkv;
+      iss_bu = iss_u;
+    }
+    const int b = iss_b, kvh = iss_kvh;
+    const int t0 = iss_ti * TOK;
+    if (++iss_ti == P.tpu) {
+      iss_ti = 0;
+      ++iss_u;
+    }
     const int s = i % Cfg::STAGES;
     const uint32_t bar = bar_base + 8 * s;
     const uint32_t dst = smem_base + s * Cfg::STAGE;
     mbar_arrive_expect_tx(bar, Cfg::TX);
-    tma_load_4d(dst, &tm_kp, bar, 0, t0, kvh, b);
-    tma_load_4d(dst + Cfg::KP, &tm_vp, bar, 0, t0, kvh, b);
+    tma_load_5d(dst, &tm_kp, bar, 0, t0, 0, kvh, b);
+    tma_load_5d(dst + Cfg::KP, &tm_vp, bar, 0, t0, 0, kvh, b);
 #pragma unroll
     for (int k = 0; k < Cfg::NSB; ++k) {
       const int x = (t0 + k * Cfg::TS) * NG;
@@ -337,21 +361,21 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
   }
 
   // ---- per-unit state --------------------------------------------------
-  uint32_t qf[NCH][2][2];       // q B-fragments (hi), [chunk][kstep][reg]
+  uint32_t qf[NCH][2][2];               // q B-fragments (hi), [chunk][kstep][reg]
   uint32_t qfl[SPLIT ? NCH : 1][2][2];  // lo parts (SPLIT only)
-  float bias[NG][2];            // -136 * sum(q) per group for cols 2tg, 2tg+1
-  float o_acc[NCH][2][4];       // O^T fragments [chunk][j][c]
-  float sp_acc[NG][4];          // sum of P' per group (for the +128 bias of V codes)
+  float bias[NG][2];                    // -136 * sum(q) per group for cols 2tg, 2tg+1
+  float o_acc[NCH][2][4];               // O^T fragments [chunk][j][c]
+  float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
   int cur_unit = -1;
-  int col_qi[2];                // query row of this lane's columns 2tg, 2tg+1
-  int64_t col_lim[2];
+  int col_lim[2];
+  int lim_min = 0;  // smallest key limit over the CTA's columns (warp-uniform)
 
   auto load_unit = [&](int u) {
     const int bk = u / P.hc, hcid = u % P.hc;
     const int b = bk / C.Hkv, kvh = bk % C.Hkv;
-    // B operand column n = g
     {
+      // B operand column n = g
       const int n = hcid * NCOL + g;
       const bool ok = n < P.ncols;
       const int qi = ok ? n / C.R : 0;
@@ -404,10 +428,15 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
     for (int j = 0; j < 2; ++j) {
       const int n = hcid * NCOL + 2 * tg + j;
       const int qi = n < P.ncols ? n / C.R : 0;
-      col_qi[j] = qi;
-      col_lim[j] = n < P.ncols ? key_limit(C, qi) : 0;
+      col_lim[j] = n < P.ncols ? static_cast<int>(key_limit(C, qi)) : 0;
       m_run[j] = kNegInf;
       l_run[j] = 0.0f;
+    }
+    {
+      // padding columns (n >= ncols) never mask real ones: treat them as unlimited
+      const int a = (hcid * NCOL + 2 * tg < P.ncols) ? col_lim[0] : INT_MAX;
+      const int b2 = (hcid * NCOL + 2 * tg + 1 < P.ncols) ? col_lim[1] : INT_MAX;
+      lim_min = __reduce_min_sync(0xffffffffu, min(a, b2));
     }
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
@@ -490,91 +519,111 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
   };
 
   const uint32_t ones = 0x3F803F80u;  // bf16x2 (1, 1)
+  // lane-constant smem offsets inside a stage (chunk-major packed layout)
+  const uint32_t k_off = (WROWS * warp + g) * 16 + 4 * tg;       // rows g (+8, +16, +24)
+  const uint32_t v_off = (WROWS * warp + 2 * tg) * 16 + 2 * g;   // rows 2tg (+1, +8, +9, +16..)
+  const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
+  int u = u_first, ti = ti_first - 1;
+  int stage = -1;
+  uint32_t phase = 1;
   for (int i = 0; i < ntiles; ++i) {
-    const int64_t gt = first_tile + i;
-    const int u = unit_of(gt);
-    const int ti = static_cast<int>(gt - static_cast<int64_t>(u) * P.tpu);
+    if (++ti == P.tpu) {
+      ti = 0;
+      ++u;
+    }
+    if (++stage == Cfg::STAGES) stage = 0;
+    if (stage == 0) phase ^= 1u;
     if (u != cur_unit) {
       load_unit(u);
       cur_unit = u;
     }
-    const int s = i % Cfg::STAGES;
-    const uint32_t phase = (i / Cfg::STAGES) & 1;
-    if (!mbar_wait_bounded(bar_base + 8 * s, phase)) {
+    if (!mbar_wait_bounded(bar_base + 8 * stage, phase)) {
       atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
       sh_abort = 1;
     }
-    const uint32_t kp = smem_base + s * Cfg::STAGE;
+    const uint32_t kp = smem_base + stage * Cfg::STAGE;
     const uint32_t vp = kp + Cfg::KP;
     const uint32_t ksb = kp + 2 * Cfg::KP;
     const uint32_t vsb = ksb + Cfg::KS;
-    const int r0 = 16 * warp + g, r1 = r0 + 8;
-    const int tok0 = ti * TOK;
+    const int tok0 = ti * TOK + WROWS * warp;  // first token row of this warp
 
-    // ---------------- scores: S^T[token][col] ---------------------------
-    float sc[NG][4];
+    // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
+    float sc[2][NG][4];
 #pragma unroll
-    for (int gi = 0; gi < NG; ++gi) {
-      sc[gi][0] = bias[gi][0];
-      sc[gi][1] = bias[gi][1];
-      sc[gi][2] = bias[gi][0];
-      sc[gi][3] = bias[gi][1];
-    }
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        sc[h][gi][0] = bias[gi][0];
+        sc[h][gi][1] = bias[gi][1];
+        sc[h][gi][2] = bias[gi][0];
+        sc[h][gi][3] = bias[gi][1];
+      }
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      const uint32_t x0 = lds32(kp + swz<Cfg::SWZ>(r0 * Cfg::P + 16 * c + 4 * tg));
-      const uint32_t x1 = lds32(kp + swz<Cfg::SWZ>(r1 * Cfg::P + 16 * c + 4 * tg));
       const int gi = c / CPG;
-      mma_bf16_16816(sc[gi], nib2(x0), nib2(x1), nib2(x0 >> 4), nib2(x1 >> 4), qf[c][0][0],
-                     qf[c][0][1]);
-      mma_bf16_16816(sc[gi], nib2(x0 >> 8), nib2(x1 >> 8), nib2(x0 >> 12), nib2(x1 >> 12),
-                     qf[c][1][0], qf[c][1][1]);
-      if constexpr (SPLIT) {
-        mma_bf16_16816(sc[gi], nib2(x0), nib2(x1), nib2(x0 >> 4), nib2(x1 >> 4), qfl[c][0][0],
-                       qfl[c][0][1]);
-        mma_bf16_16816(sc[gi], nib2(x0 >> 8), nib2(x1 >> 8), nib2(x0 >> 12), nib2(x1 >> 12),
-                       qfl[c][1][0], qfl[c][1][1]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t base = kp + c * Cfg::CH + k_off + h * 256;
+        const uint32_t x0 = lds32(base), x1 = lds32(base + 128);
+        const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
+        const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
+        mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
+        mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
+        if constexpr (SPLIT) {
+          mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
+          mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
+        }
       }
     }
-    float ks0[NG], ks1[NG], vs0[NG], vs1[NG];
-    scales_row<NG, ST>(ksb + r0 * Cfg::SROW, ks0);
-    scales_row<NG, ST>(ksb + r1 * Cfg::SROW, ks1);
-    scales_row<NG, ST>(vsb + r0 * Cfg::SROW, vs0);
-    scales_row<NG, ST>(vsb + r1 * Cfg::SROW, vs1);
-    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;  // [row r0/r1][col 2tg / 2tg+1]
+    // s[h][r][cc]: sub-tile h, row g (r=0) / g+8 (r=1), column 2tg+cc
+    float s[2][2][2];
+    float vsc[2][2][NG];
 #pragma unroll
-    for (int gi = 0; gi < NG; ++gi) {
-      s00 = fmaf(ks0[gi], sc[gi][0], s00);
-      s01 = fmaf(ks0[gi], sc[gi][1], s01);
-      s10 = fmaf(ks1[gi], sc[gi][2], s10);
-      s11 = fmaf(ks1[gi], sc[gi][3], s11);
-    }
-    s00 *= C.scale_log2; s01 *= C.scale_log2; s10 *= C.scale_log2; s11 *= C.scale_log2;
-    {
-      const int64_t t_r0 = tok0 + r0, t_r1 = tok0 + r1;
-      if (t_r0 >= col_lim[0]) s00 = kNegInf;
-      if (t_r0 >= col_lim[1]) s01 = kNegInf;
-      if (t_r1 >= col_lim[0]) s10 = kNegInf;
-      if (t_r1 >= col_lim[1]) s11 = kNegInf;
-    }
-    // ---------------- online softmax (per column, lazy rescale) ---------
-    float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int o = 4; o <= 16; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      for (int r = 0; r < 2; ++r) {
+        float ks[NG];
+        scales_row<NG, ST>(ksb + s_row0 + (16 * h + 8 * r) * Cfg::SROW, ks);
+        scales_row<NG, ST>(vsb + s_row0 + (16 * h + 8 * r) * Cfg::SROW, vsc[h][r]);
+        float a = 0.f, b2 = 0.f;
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          a = fmaf(ks[gi], sc[h][gi][2 * r], a);
+          b2 = fmaf(ks[gi], sc[h][gi][2 * r + 1], b2);
+        }
+        s[h][r][0] = a * C.scale_log2;
+        s[h][r][1] = b2 * C.scale_log2;
+      }
+    if (tok0 + WROWS > lim_min) {  // only rows that reach past a key limit need masks
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int t = tok0 + 16 * h + 8 * r + g;
+          if (t >= col_lim[0]) s[h][r][0] = kNegInf;
+          if (t >= col_lim[1]) s[h][r][1] = kNegInf;
+        }
     }
-    const bool need = (mx0 > m_run[0] + 8.0f) || (mx1 > m_run[1] + 8.0f);
+    // ---------------- online softmax over 32 rows (lazy rescale) --------
+    float mx[2];
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      mx[cc] = fmaxf(fmaxf(s[0][0][cc], s[0][1][cc]), fmaxf(s[1][0][cc], s[1][1][cc]));
+#pragma unroll
+      for (int o = 4; o <= 16; o <<= 1)
+        mx[cc] = fmaxf(mx[cc], __shfl_xor_sync(0xffffffffu, mx[cc], o));
+    }
+    const bool need = (mx[0] > m_run[0] + 8.0f) || (mx[1] > m_run[1] + 8.0f);
     if (__any_sync(0xffffffffu, need)) {
       float alpha[2];
-      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-      alpha[0] = (mn0 == kNegInf) ? 1.0f : fast_exp2(m_run[0] - mn0);
-      alpha[1] = (mn1 == kNegInf) ? 1.0f : fast_exp2(m_run[1] - mn1);
-      m_run[0] = mn0;
-      m_run[1] = mn1;
-      l_run[0] *= alpha[0];
-      l_run[1] *= alpha[1];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const float mn = fmaxf(m_run[cc], mx[cc]);
+        alpha[cc] = (mn == kNegInf) ? 1.0f : fast_exp2(m_run[cc] - mn);
+        m_run[cc] = mn;
+        l_run[cc] *= alpha[cc];
+      }
 #pragma unroll
       for (int c = 0; c < NCH; ++c)
 #pragma unroll
@@ -592,58 +641,62 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 4))
         sp_acc[gi][3] *= alpha[1];
       }
     }
-    const float me0 = (m_run[0] == kNegInf) ? 0.0f : m_run[0];
-    const float me1 = (m_run[1] == kNegInf) ? 0.0f : m_run[1];
-    const float p00 = fast_exp2(s00 - me0), p01 = fast_exp2(s01 - me1);
-    const float p10 = fast_exp2(s10 - me0), p11 = fast_exp2(s11 - me1);
-    l_run[0] += p00 + p10;
-    l_run[1] += p01 + p11;
+    const float me[2] = {(m_run[0] == kNegInf) ? 0.0f : m_run[0],
+                         (m_run[1] == kNegInf) ? 0.0f : m_run[1]};
+    float p[2][2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          p[h][r][cc] = fast_exp2(s[h][r][cc] - me[cc]);
+          l_run[cc] += p[h][r][cc];
+        }
 
-    // ---------------- P' = P * v_scale per group, as B fragments --------
-    uint32_t pb[NG][2];
-    uint32_t pbl[SPLIT ? NG : 1][2];
+    // ---------------- per sub-tile: P' = P * v_scale, then O^T += V^T P' -
 #pragma unroll
-    for (int gi = 0; gi < NG; ++gi) {
-      const float a0 = p00 * vs0[gi], a1 = p01 * vs0[gi];
-      const float c0 = p10 * vs1[gi], c1 = p11 * vs1[gi];
-      const uint32_t u0 = pack_bf16x2(a0, a1);
-      const uint32_t u1 = pack_bf16x2(c0, c1);
-      pb[gi][0] = movmatrix_trans(u0);
-      pb[gi][1] = movmatrix_trans(u1);
-      if constexpr (SPLIT) {
-        const uint32_t l0 = pack_bf16x2(a0 - bf16lo_to_f32(u0), a1 - bf16hi_to_f32(u0));
-        const uint32_t l1 = pack_bf16x2(c0 - bf16lo_to_f32(u1), c1 - bf16hi_to_f32(u1));
-        pbl[gi][0] = movmatrix_trans(l0);
-        pbl[gi][1] = movmatrix_trans(l1);
+    for (int h = 0; h < 2; ++h) {
+      uint32_t pb[NG][2];
+      uint32_t pbl[SPLIT ? NG : 1][2];
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        const float a0 = p[h][0][0] * vsc[h][0][gi], a1 = p[h][0][1] * vsc[h][0][gi];
+        const float c0 = p[h][1][0] * vsc[h][1][gi], c1 = p[h][1][1] * vsc[h][1][gi];
+        const uint32_t u0 = pack_bf16x2(a0, a1);
+        const uint32_t u1 = pack_bf16x2(c0, c1);
+        pb[gi][0] = movmatrix_trans(u0);
+        pb[gi][1] = movmatrix_trans(u1);
+        if constexpr (SPLIT) {
+          const uint32_t l0 = pack_bf16x2(a0 - bf16lo_to_f32(u0), a1 - bf16hi_to_f32(u0));
+          const uint32_t l1 = pack_bf16x2(c0 - bf16lo_to_f32(u1), c1 - bf16hi_to_f32(u1));
+          pbl[gi][0] = movmatrix_trans(l0);
+          pbl[gi][1] = movmatrix_trans(l1);
+        }
       }
-    }
-    // ---------------- O^T[dim][col] += V^T . P' -------------------------
-    const int ra = 16 * warp + 2 * tg;
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const uint32_t ha = lds16(vp + swz<Cfg::SWZ>(ra * Cfg::P + 16 * c + 2 * g));
-      const uint32_t hb = lds16(vp + swz<Cfg::SWZ>((ra + 1) * Cfg::P + 16 * c + 2 * g));
-      const uint32_t hc = lds16(vp + swz<Cfg::SWZ>((ra + 8) * Cfg::P + 16 * c + 2 * g));
-      const uint32_t hd = lds16(vp + swz<Cfg::SWZ>((ra + 9) * Cfg::P + 16 * c + 2 * g));
-      const uint32_t wab = prmt(ha, hb, 0x5410);
-      const uint32_t wcd = prmt(hc, hd, 0x5410);
-      const int gi = c / CPG;
-      mma_bf16_16816(o_acc[c][0], nib2(wab), nib2(wab >> 4), nib2(wcd), nib2(wcd >> 4),
-                     pb[gi][0], pb[gi][1]);
-      mma_bf16_16816(o_acc[c][1], nib2(wab >> 8), nib2(wab >> 12), nib2(wcd >> 8),
-                     nib2(wcd >> 12), pb[gi][0], pb[gi][1]);
-      if constexpr (SPLIT) {
-        mma_bf16_16816(o_acc[c][0], nib2(wab), nib2(wab >> 4), nib2(wcd), nib2(wcd >> 4),
-                       pbl[gi][0], pbl[gi][1]);
-        mma_bf16_16816(o_acc[c][1], nib2(wab >> 8), nib2(wab >> 12), nib2(wcd >> 8),
-                       nib2(wcd >> 12), pbl[gi][0], pbl[gi][1]);
+      for (int c = 0; c < NCH; ++c) {
+        const uint32_t base = vp + c * Cfg::CH + v_off + h * 256;
+        const uint32_t ha = lds16(base), hb = lds16(base + 16);
+        const uint32_t hc = lds16(base + 128), hd = lds16(base + 144);
+        const uint32_t wab = prmt(ha, hb, 0x5410);
+        const uint32_t wcd = prmt(hc, hd, 0x5410);
+        const int gi = c / CPG;
+        const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
+        const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
+        mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pb[gi][0], pb[gi][1]);
+        mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pb[gi][0], pb[gi][1]);
+        if constexpr (SPLIT) {
+          mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pbl[gi][0], pbl[gi][1]);
+          mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pbl[gi][0], pbl[gi][1]);
+        }
       }
-    }
 #pragma unroll
-    for (int gi = 0; gi < NG; ++gi) {
-      mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
-      if constexpr (SPLIT)
-        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pbl[gi][0], pbl[gi][1]);
+      for (int gi = 0; gi < NG; ++gi) {
+        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
+        if constexpr (SPLIT)
+          mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pbl[gi][0], pbl[gi][1]);
+      }
     }
 
     // ---------------- release the stage, refill, flush at unit end ------
@@ -801,10 +854,14 @@ static bool fast_eligible(const kv4_tensor *q, const kv4_tensor *kp, const kv4_t
   if (!(S.d == 64 || S.d == 128 || S.d == 256)) return false;
   if (!(S.G == 32 || S.G == 64 || S.G == 128) || S.G > S.d || S.d % S.G) return false;
   if (S.sk <= 0 || S.sk >= (1LL << 31) / 8) return false;
+  if (S.B * S.Hkv * ((S.Hq / S.Hkv * S.sq + NCOL - 1) / NCOL) * ((S.sk + TOK - 1) / TOK) >=
+      (1LL << 31))
+    return false;
   const int64_t ng = S.d / S.G;
   const int ss = dtype_size(ks->dtype);
   for (const kv4_tensor *t : {kp, vp}) {
-    if (!aligned16(t->data) || t->stride[3] != 1 || t->stride[2] % 16) return false;
+    if (!aligned16(t->data) || t->stride[3] != 1 || t->stride[2] % 16 || t->shape[3] % 16)
+      return false;
     if (t->shape[1] > 1 && t->stride[1] % 16) return false;
     if (t->shape[0] > 1 && t->stride[0] % 16) return false;
   }
@@ -901,24 +958,24 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
   }
 }
 
-static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int box_inner, int swz_bytes) {
+// Packed K/V map: 5-D view {16 B, token, 16-B chunk, head, batch} so that a
+// box lands in shared memory chunk-major ([chunk][token][16 B]).
+static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int nch, int tokens) {
   auto enc = get_encode();
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t->shape[3]), static_cast<cuuint64_t>(t->shape[2]),
+  const int64_t sh = t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2];
+  const int64_t sb = t->shape[0] > 1 ? t->stride[0] : sh * t->shape[1];
+  cuuint64_t dims[5] = {16, static_cast<cuuint64_t>(t->shape[2]),
+                        static_cast<cuuint64_t>(t->shape[3] / 16),
                         static_cast<cuuint64_t>(t->shape[1]),
                         static_cast<cuuint64_t>(t->shape[0])};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t->stride[2]),
-                           static_cast<cuuint64_t>(t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2]),
-                           static_cast<cuuint64_t>(t->shape[0] > 1 ? t->stride[0] : (t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2]) * t->shape[1])};
-  // strides must be multiples of 16 even for size-1 dims; round the synthetic ones up
-  for (int i = 0; i < 3; ++i) strides[i] = (strides[i] + 15) / 16 * 16;
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(TOK), 1, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  CUtensorMapSwizzle sw = swz_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
-                          : swz_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                            : CU_TENSOR_MAP_SWIZZLE_128B;
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, t->data, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(t->stride[2]), 16,
+                           static_cast<cuuint64_t>((sh + 15) / 16 * 16),
+                           static_cast<cuuint64_t>((sb + 15) / 16 * 16)};
+  cuuint32_t box[5] = {16, static_cast<cuuint32_t>(tokens), static_cast<cuuint32_t>(nch), 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, t->data, dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
 }
 
@@ -950,8 +1007,8 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
   using Cfg = FastCfg<D, G, ST>;
   CUtensorMap tkp, tvp, tks, tvs;
   int rc;
-  if ((rc = encode_packed(&tkp, kp, Cfg::P, Cfg::P))) return rc;
-  if ((rc = encode_packed(&tvp, vp, Cfg::P, Cfg::P))) return rc;
+  if ((rc = encode_packed(&tkp, kp, Cfg::NCH, TOK))) return rc;
+  if ((rc = encode_packed(&tvp, vp, Cfg::NCH, TOK))) return rc;
   if ((rc = encode_scales(&tks, ks, Cfg::TS))) return rc;
   if ((rc = encode_scales(&tvs, vs, Cfg::TS))) return rc;
   occupancy_of<D, G, ST, SPLIT>();  // sets the smem attribute once

@@ -126,7 +126,7 @@ def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, s
                            **kw) -> None:
     L = lib()
     ds = [desc(t) for t in (q, kp, ks, vp, vs, part_o)]
-    dl = desc(part_lse)
+    dl = desc(part_lse.unsqueeze(-1) if part_lse.dim() == q.dim() - 1 else part_lse)
     o = _opts(**kw)
     optr = ctypes.byref(o) if o else None
     p = AttnPlan()

@@ -14,17 +14,26 @@ from helpers import ATOL, f32, kv_inputs, oracle_attention
 pytestmark = pytest.mark.gpu
 
 
-def _run(b, hq, hkv, sq, sk, d, gs, qdt, causal=False, seed=0, sdt=None, **kw):
+def _run(b, hq, hkv, sq, sk, d, gs, qdt, causal=False, seed=0, sdt=None, contiguous=False,
+         **kw):
+    """Quantize seeded K/V into a capacity-buffer cache (or contiguous tensors),
+    run the kernel and the oracle."""
     from kernels.llama3.attention_quant import attention_forward_quant_gqa
     from kernels.llama3.quantize import quantize_int4
     from kvint4 import frontend
+    from kvint4.cache import Int4KVStore
     k, v = kv_inputs(b, hkv, sk, d, dtype=qdt, seed=seed, device="cuda")
     g = torch.Generator().manual_seed(seed + 100)
     q = torch.randn(b, hq, sq, d, generator=g).to(qdt).cuda()
-    kp, ks = quantize_int4(k, gs)
-    vp, vs = quantize_int4(v, gs)
-    if sdt is not None:
-        ks, vs = ks.to(sdt), vs.to(sdt)
+    if contiguous:
+        kp, ks = quantize_int4(k, gs)
+        vp, vs = quantize_int4(v, gs)
+        if sdt is not None:
+            ks, vs = ks.to(sdt), vs.to(sdt)
+    else:
+        store = Int4KVStore(gs, scale_dtype=sdt)
+        store.append(k, v, 0)
+        kp, ks, vp, vs = store.layer(0).views()
     if kw:
         out = frontend.attention(q, kp, ks, vp, vs, n_q_heads=hq, n_kv_heads=hkv,
                                  group_size=gs, is_causal=causal, **kw)
@@ -76,6 +85,16 @@ def test_stream_k_split_invariance(tiles_per_cta):
 def test_multi_query_rows_causal_bottom_right(sq, causal):
     q, cache, out, ref = _run(1, 8, 2, sq, 90, 128, 32, torch.float32, causal=causal, seed=sq)
     np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+
+
+@pytest.mark.parametrize("sk", [77, 301, 4096])
+def test_contiguous_tensors_any_length(sk):
+    """Freshly quantized contiguous tensors (the reference API's usual input):
+    aligned lengths take the TMA path, others the generic kernel; both agree
+    with the oracle."""
+    q, cache, out, ref = _run(2, 8, 2, 1, sk, 128, 32, torch.bfloat16, contiguous=True)
+    assert _plan_path(q, cache, 32) == (1 if sk % 2 == 0 else 2)
+    np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
 
 
 def test_generic_path_matches_oracle():

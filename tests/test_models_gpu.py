@@ -73,38 +73,39 @@ def test_llama_cache_tracks_seq_len_and_bytes():
     assert cache.nbytes() < baseline / 2
 
 
+def _greedy(model, prompt, cache, n_new):
+    tokens = []
+    with torch.no_grad():
+        out = model(input_ids=prompt, past_key_values=cache, use_cache=True)
+        nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
+        tokens.append(int(nxt.item()))
+        for _ in range(n_new - 1):
+            out = model(input_ids=nxt, past_key_values=cache, use_cache=True)
+            nxt = out.logits[:, -1, :].argmax(-1, keepdim=True)
+            tokens.append(int(nxt.item()))
+    return tokens
+
+
 def test_llama_greedy_generate_prefix_agreement():
-    """Greedy prefix agreement >= 4 of 16 tokens (reference
-    tests/llama3/test_llama3_generate_parity.py:52-74), batch 2."""
+    """Greedy prefix agreement >= 4 of 16 tokens, same model, seeds and prompt as
+    the reference's tests/llama3/test_llama3_generate_parity.py:52-74."""
     from models.llama3.kv_cache import QuantizedKVCache
     from models.llama3.llama3_quant import replace_llama_attention_with_quantized
     dev = torch.device("cuda")
     model_ref = _tiny_llama(dev)
     model_q = _tiny_llama(dev)
     model_q.load_state_dict(model_ref.state_dict())
-    replace_llama_attention_with_quantized(model_q)
-    prompt = torch.randint(0, 256, (2, 24), device=dev, generator=torch.Generator(
-        device="cuda").manual_seed(7))
-
-    def greedy(model, cache):
-        toks = []
-        with torch.no_grad():
-            out = model(input_ids=prompt, past_key_values=cache, use_cache=True)
-            for _ in range(16):
-                nxt = out.logits[:, -1].argmax(-1, keepdim=True)
-                toks.append(nxt)
-                out = model(input_ids=nxt, past_key_values=cache, use_cache=True)
-        return torch.cat(toks, 1)
-
-    a = greedy(model_ref, DynamicCache())
-    b = greedy(model_q, QuantizedKVCache())
-    for row in range(2):
-        agree = 0
-        for x, y in zip(a[row].tolist(), b[row].tolist()):
-            if x != y:
-                break
-            agree += 1
-        assert agree >= 4
+    replace_llama_attention_with_quantized(model_q, group_size=32)
+    torch.manual_seed(321)
+    prompt = torch.randint(0, 256, (1, 24), device=dev, dtype=torch.long)
+    a = _greedy(model_ref, prompt, DynamicCache(), 16)
+    b = _greedy(model_q, prompt, QuantizedKVCache(group_size=32), 16)
+    agree = 0
+    for x, y in zip(a, b):
+        if x != y:
+            break
+        agree += 1
+    assert agree >= 4, (a, b)
 
 
 def test_gpt2_random_decode_matches_dynamic_cache():
