@@ -74,7 +74,7 @@ typedef struct kv4_attn_plan {
   int32_t tiles_per_cta;   /* stream-K chunk (fast path) */
   int32_t units;           /* (batch, kv head, column chunk) work units */
   int32_t max_parts;       /* partial slots per unit */
-  int32_t kernels;         /* kernel launches one call makes (1 or 2) */
+  int32_t kernels;         /* kernel launches one call makes */
   int64_t workspace_bytes; /* bytes the call needs in `workspace` */
 } kv4_attn_plan;
 
@@ -124,7 +124,12 @@ int kv4_dequantize(const kv4_tensor *packed, const kv4_tensor *scales, const kv4
  * Query head h reads KV head h / (Hq/Hkv); with is_causal, query row i sees
  * keys j <= sk - sq + i (bottom-right).  sm_scale <= 0 means d^-1/2.
  * `workspace` (device, >= kv4_attention_plan().workspace_bytes) holds
- * split-sequence partials; it may be NULL when that size is 0.
+ * split-sequence partials (written from the front) and per-unit counters
+ * (the LAST plan.units * 4 bytes of the `workspace_bytes` given); it may be
+ * NULL when the planned size is 0.  The counter bytes must be zero before
+ * the call and are zero again when it completes, so keep partial data of
+ * other calls out of them (e.g. reserve a fixed zeroed tail).  Calls sharing
+ * a workspace must not overlap on the GPU.
  * Replaces kernels/llama3/attention_quant.py:159-286
  * (attention_forward_quant_gqa) and kernels/gpt2/attention_quant.py:140-248
  * (attention_forward_quant, Hq == Hkv).

@@ -15,8 +15,9 @@
 //    operands in registers; per-group scales are applied exactly in fp32
 //    (K: after a per-group partial dot product; V: folded into P).  The grid
 //    is persistent and stream-K balanced over (unit, token tile) work;
-//    units split across CTAs leave (o, lse) partials that a second small
-//    kernel merges with a log-sum-exp reduction.
+//    units split across CTAs leave (o, lse) partials in the workspace, and
+//    the last CTA to finish a unit (per-unit counter) merges them with a
+//    log-sum-exp reduction -- one launch per call.
 //  * generic (kv4_attn_generic): a warp-per-token FFMA kernel for any shape,
 //    dtype, stride, group size and long query blocks.
 #include <cuda.h>
@@ -191,12 +192,14 @@ struct FastParams {
   int maxp;       // partial slots per unit
   float *ws_o;    // [units*maxp][NCOL][d]
   float *ws_lse;  // [units*maxp][NCOL]   (log2 domain)
+  int *counters;  // [units] finished-segment counts (zero between calls)
 };
 
-// Shared-memory layout of one stage (per tensor): packed codes chunk-major,
-// [chunk (16 B = 32 dims)][token][16 B], so that every fragment load is a
-// lane-constant base plus an immediate and all accesses are bank-conflict
-// free; scales token-major [token][group].
+// Shared-memory layout of one stage (per tensor): packed codes token-major
+// [token][P bytes] as TMA writes them with the P-byte swizzle (16-byte chunk c
+// of row r lands at chunk c ^ ((r >> SH) & SWZ)); scales token-major
+// [token][group].  Every row a lane reads has the same XOR key, so the
+// swizzle folds into lane-constant chunk offsets.
 template <int D, int G, typename ST>
 struct FastCfg {
   static constexpr int P = D / 2;             // packed bytes per token
@@ -204,7 +207,8 @@ struct FastCfg {
   static constexpr int NG = D / G;            // scale groups per token
   static constexpr int CPG = G / 32;          // chunks per group
   static constexpr int SROW = NG * (int)sizeof(ST);  // scale bytes per token
-  static constexpr int CH = TOK * 16;         // bytes of one chunk plane
+  static constexpr int SWZ = (P == 32) ? 1 : (P == 64) ? 3 : 7;  // XOR key mask
+  static constexpr int SH = (P == 32) ? 2 : (P == 64) ? 1 : 0;    // row -> key shift
   static constexpr int KP = TOK * P;          // packed bytes per stage per tensor
   static constexpr int KS = TOK * SROW;       // scale bytes per stage per tensor
   static constexpr int TS = (TOK * NG <= 256) ? TOK : 256 / NG;  // tokens per scale TMA box
@@ -212,7 +216,8 @@ struct FastCfg {
   static constexpr int STAGE = ((2 * KP + 2 * KS) + 1023) / 1024 * 1024;
   static constexpr int STAGES = (D == 256) ? 2 : 3;
   static constexpr int MERGE = NWARP * NCOL * D * 4;
-  static constexpr int SMEM = STAGES * STAGE + MERGE + 2 * NWARP * NCOL * 4 + 64 + 1024;
+  static constexpr int SMEM = STAGES * STAGE + MERGE + 3 * NWARP * NCOL * 4 + 2 * NCOL * 4 +
+                              16 * STAGES + 1024;
   static constexpr uint32_t TX = 2 * KP + 2 * KS;
 };
 
@@ -294,8 +299,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   float *merge_o = reinterpret_cast<float *>(smem + Cfg::STAGES * Cfg::STAGE);
   float *merge_m = merge_o + NWARP * NCOL * D;
   float *merge_l = merge_m + NWARP * NCOL;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(merge_l + NWARP * NCOL);
+  float *merge_f = merge_l + NWARP * NCOL;
+  float *merge_lse = merge_f + NWARP * NCOL;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(merge_lse + 2 * NCOL);  // full[S], empty[S]
   __shared__ int sh_abort;
+  __shared__ int sh_last;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -315,7 +323,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     prefetch_tmap(&tm_vp);
     prefetch_tmap(&tm_ks);
     prefetch_tmap(&tm_vs);
-    for (int s = 0; s < Cfg::STAGES; ++s) mbar_init(bar_base + 8 * s, 1);
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(bar_base + 8 * s, 1);                            // full: producer + tx
+      mbar_init(bar_base + 8 * (Cfg::STAGES + s), NWARP);        // empty: one per warp
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -344,8 +355,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     const uint32_t bar = bar_base + 8 * s;
     const uint32_t dst = smem_base + s * Cfg::STAGE;
     mbar_arrive_expect_tx(bar, Cfg::TX);
-    tma_load_5d(dst, &tm_kp, bar, 0, t0, 0, kvh, b);
-    tma_load_5d(dst + Cfg::KP, &tm_vp, bar, 0, t0, 0, kvh, b);
+    tma_load_4d(dst, &tm_kp, bar, 0, t0, kvh, b);
+    tma_load_4d(dst + Cfg::KP, &tm_vp, bar, 0, t0, kvh, b);
 #pragma unroll
     for (int k = 0; k < Cfg::NSB; ++k) {
       const int x = (t0 + k * Cfg::TS) * NG;
@@ -450,13 +461,15 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       for (int e = 0; e < 4; ++e) sp_acc[gi][e] = 0.0f;
   };
 
-  // finish the current unit segment: merge warps through smem, write output
+  // Finish the current unit segment: merge the 4 warps through smem, then
+  // either write the output (unit wholly inside this CTA) or write a partial
+  // slot; the last CTA to finish a split unit (per-unit counter) merges all
+  // of the unit's slots and writes the output, then re-arms the counter.
   auto flush = [&](int u) {
     const int bk = u / P.hc, hcid = u % P.hc;
     const int b = bk / C.Hkv, kvh = bk % C.Hkv;
-    // l over the 8 token-row lanes
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < 2; ++j) {  // l over the 8 token-row lanes
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
@@ -485,43 +498,102 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
     }
     __syncthreads();
-    const int64_t ft = static_cast<int64_t>(u) * P.tpu;
-    const int first_cta = static_cast<int>(ft / P.L);
-    const int last_cta = static_cast<int>((ft + P.tpu - 1) / P.L);
+    const int ft = u * P.tpu;
+    const int first_cta = ft / P.L;
+    const int last_cta = (ft + P.tpu - 1) / P.L;
     const bool whole = first_cta == last_cta;
     const int slot = u * P.maxp + (static_cast<int>(blockIdx.x) - first_cta);
+    if (tid < NCOL) {  // per-column warp weights (already divided by the total l)
+      float M = kNegInf;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) M = fmaxf(M, merge_m[w * NCOL + tid]);
+      float f[NWARP], Lsum = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) {
+        f[w] = (M == kNegInf) ? 0.0f : exp2f(merge_m[w * NCOL + tid] - M);
+        Lsum += merge_l[w * NCOL + tid] * f[w];
+      }
+      const float inv = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) merge_f[w * NCOL + tid] = f[w] * inv;
+      merge_lse[tid] = Lsum > 0.0f ? M + log2f(Lsum) : kNegInf;
+    }
+    __syncthreads();
     for (int idx = tid; idx < NCOL * D; idx += blockDim.x) {
       const int col = idx / D, dd = idx % D;
       const int n = hcid * NCOL + col;
       if (n >= P.ncols) continue;
-      float M = kNegInf;
+      float val = 0.0f;
 #pragma unroll
-      for (int w = 0; w < NWARP; ++w) M = fmaxf(M, merge_m[w * NCOL + col]);
-      float Lsum = 0.0f, o = 0.0f;
-#pragma unroll
-      for (int w = 0; w < NWARP; ++w) {
-        const float f = (M == kNegInf) ? 0.0f : exp2f(merge_m[w * NCOL + col] - M);
-        Lsum += merge_l[w * NCOL + col] * f;
-        o += merge_o[(w * NCOL + col) * D + dd] * f;
-      }
-      const float val = Lsum > 0.0f ? o / Lsum : 0.0f;
-      const float lse = Lsum > 0.0f ? M + log2f(Lsum) : kNegInf;
+      for (int w = 0; w < NWARP; ++w) val += merge_o[(w * NCOL + col) * D + dd] * merge_f[w * NCOL + col];
       const int qi = n / C.R, h = kvh * C.R + n % C.R;
       if (whole) {
         emit_value(C, b, h, qi, dd, val);
-        if (dd == 0) emit_lse(C, b, h, qi, lse);
+        if (dd == 0) emit_lse(C, b, h, qi, merge_lse[col]);
       } else {
         P.ws_o[(static_cast<int64_t>(slot) * NCOL + col) * D + dd] = val;
-        if (dd == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = lse;
+        if (dd == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = merge_lse[col];
+      }
+    }
+    if (!whole) {
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        const int nparts = last_cta - first_cta + 1;
+        const int prev = atomicAdd(&P.counters[u], 1);
+        sh_last = (prev == nparts - 1);
+        if (sh_last) P.counters[u] = 0;  // re-arm for the next call
+      }
+      __syncthreads();
+      if (sh_last) {
+        __threadfence();
+        const int nparts = last_cta - first_cta + 1;
+        const int64_t slot0 = static_cast<int64_t>(u) * P.maxp;
+        if (tid < NCOL) {
+          float M = kNegInf;
+          for (int p = 0; p < nparts; ++p) M = fmaxf(M, __ldcg(&P.ws_lse[(slot0 + p) * NCOL + tid]));
+          float W = 0.0f;
+          for (int p = 0; p < nparts; ++p)
+            W += (M == kNegInf) ? 0.0f : exp2f(__ldcg(&P.ws_lse[(slot0 + p) * NCOL + tid]) - M);
+          merge_m[tid] = M;
+          merge_l[tid] = W > 0.0f ? 1.0f / W : 0.0f;
+          merge_lse[tid] = W > 0.0f ? M + log2f(W) : kNegInf;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < NCOL * D; idx += blockDim.x) {
+          const int col = idx / D, dd = idx % D;
+          const int n = hcid * NCOL + col;
+          if (n >= P.ncols) continue;
+          const float M = merge_m[col];
+          float o = 0.0f;
+          if (M != kNegInf)
+            for (int p = 0; p < nparts; ++p) {
+              const float w = exp2f(__ldcg(&P.ws_lse[(slot0 + p) * NCOL + col]) - M);
+              o += w * __ldcg(&P.ws_o[((slot0 + p) * NCOL + col) * D + dd]);
+            }
+          const int qi = n / C.R, h = kvh * C.R + n % C.R;
+          emit_value(C, b, h, qi, dd, o * merge_l[col]);
+          if (dd == 0) emit_lse(C, b, h, qi, merge_lse[col]);
+        }
       }
     }
     __syncthreads();
   };
 
   const uint32_t ones = 0x3F803F80u;  // bf16x2 (1, 1)
-  // lane-constant smem offsets inside a stage (chunk-major packed layout)
-  const uint32_t k_off = (WROWS * warp + g) * 16 + 4 * tg;       // rows g (+8, +16, +24)
-  const uint32_t v_off = (WROWS * warp + 2 * tg) * 16 + 2 * g;   // rows 2tg (+1, +8, +9, +16..)
+  // Lane-constant smem offsets inside a stage.  K rows 32w+16h+g (+8) share
+  // the swizzle key of row g; V rows 32w+16h+2tg (+1, +8, +9) that of row 2tg.
+  constexpr int P_ = Cfg::P;
+  const int kkey = ((WROWS * warp + g) >> Cfg::SH) & Cfg::SWZ;
+  // (with 128-byte rows the odd V rows 2tg+1, 2tg+9 carry key ^ 1)
+  const int vkey = ((WROWS * warp + 2 * tg) >> Cfg::SH) & Cfg::SWZ;
+  constexpr int VODD = (Cfg::SH == 0) ? 1 : 0;
+  uint32_t k_off[NCH], v_off[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    k_off[c] = (WROWS * warp + g) * P_ + 16 * (c ^ kkey) + 4 * tg;
+    v_off[c] = (WROWS * warp + 2 * tg) * P_ + 16 * (c ^ vkey) + 2 * g;
+  }
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
   int u = u_first, ti = ti_first - 1;
@@ -538,9 +610,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       load_unit(u);
       cur_unit = u;
     }
-    if (!mbar_wait_bounded(bar_base + 8 * stage, phase)) {
+    if (!*reinterpret_cast<volatile int *>(&sh_abort) &&
+        !mbar_wait_bounded(bar_base + 8 * stage, phase)) {
       atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
-      sh_abort = 1;
+      sh_abort = 1;  // later waits are skipped; results are garbage, the flag reports it
     }
     const uint32_t kp = smem_base + stage * Cfg::STAGE;
     const uint32_t vp = kp + Cfg::KP;
@@ -564,8 +637,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       const int gi = c / CPG;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t base = kp + c * Cfg::CH + k_off + h * 256;
-        const uint32_t x0 = lds32(base), x1 = lds32(base + 128);
+        const uint32_t base = kp + k_off[c] + h * 16 * P_;
+        const uint32_t x0 = lds32(base), x1 = lds32(base + 8 * P_);
         const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
         const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
         mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
@@ -676,9 +749,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        const uint32_t base = vp + c * Cfg::CH + v_off + h * 256;
-        const uint32_t ha = lds16(base), hb = lds16(base + 16);
-        const uint32_t hc = lds16(base + 128), hd = lds16(base + 144);
+        const uint32_t base = vp + v_off[c] + h * 16 * P_;
+        const uint32_t base1 = vp + v_off[c ^ VODD] + h * 16 * P_;  // odd rows
+        const uint32_t ha = lds16(base), hb = lds16(base1 + P_);
+        const uint32_t hc = lds16(base + 8 * P_), hd = lds16(base1 + 9 * P_);
         const uint32_t wab = prmt(ha, hb, 0x5410);
         const uint32_t wcd = prmt(hc, hd, 0x5410);
         const int gi = c / CPG;
@@ -700,15 +774,24 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     }
 
     // ---------------- release the stage, refill, flush at unit end ------
-    __syncthreads();
-    if (sh_abort) break;
-    if (tid == 0 && i + Cfg::STAGES < ntiles) issue(i + Cfg::STAGES);
+    // Each warp frees the stage on its "empty" barrier; thread 0 refills it
+    // once all four warps are done, so warps are not locked in step.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_base + 8 * (Cfg::STAGES + stage));
+    if (tid == 0 && i + Cfg::STAGES < ntiles) {
+      if (!*reinterpret_cast<volatile int *>(&sh_abort) &&
+          !mbar_wait_bounded(bar_base + 8 * (Cfg::STAGES + stage), phase)) {
+        atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
+        sh_abort = 1;
+      }
+      issue(i + Cfg::STAGES);
+    }
     const bool unit_end = (ti == P.tpu - 1) || (i == ntiles - 1);
     if (unit_end) flush(u);
   }
   if (sh_abort && tid == 0) {
-    // drain: wait (bounded) for every load this CTA may still have in flight
-    for (int i = 0; i < ntiles; ++i) {
+    // drain: wait (bounded) for the loads this CTA may still have in flight
+    for (int i = max(0, ntiles - Cfg::STAGES); i < ntiles; ++i) {
       const int s = i % Cfg::STAGES;
       mbar_wait_bounded(bar_base + 8 * s, (i / Cfg::STAGES) & 1, 1u << 16);
     }
@@ -716,44 +799,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
 }
 
 // ===========================================================================
-// merge of stream-K partials (within one launch) and of shard partials
+// merge of shard partials (multi-GPU sequence sharding)
 // ===========================================================================
-__global__ void __launch_bounds__(128) kv4_merge_slots(const FastParams P) {
-  const AttnCommon &C = P.c;
-  const int u = blockIdx.x;
-  const int col = blockIdx.y;
-  const int D = C.d;
-  const int64_t ft = static_cast<int64_t>(u) * P.tpu;
-  const int first_cta = static_cast<int>(ft / P.L);
-  const int last_cta = static_cast<int>((ft + P.tpu - 1) / P.L);
-  if (first_cta == last_cta) return;
-  const int bk = u / P.hc, hcid = u % P.hc;
-  const int b = bk / C.Hkv, kvh = bk % C.Hkv;
-  const int n = hcid * NCOL + col;
-  if (n >= P.ncols) return;
-  const int nparts = last_cta - first_cta + 1;
-  const int64_t slot0 = static_cast<int64_t>(u) * P.maxp;
-  float M = kNegInf;
-  for (int p = 0; p < nparts; ++p) M = fmaxf(M, P.ws_lse[(slot0 + p) * NCOL + col]);
-  float W = 0.0f;
-  for (int p = 0; p < nparts; ++p) {
-    const float lp = P.ws_lse[(slot0 + p) * NCOL + col];
-    W += (M == kNegInf) ? 0.0f : exp2f(lp - M);
-  }
-  const float invW = W > 0.0f ? 1.0f / W : 0.0f;
-  const int qi = n / C.R, h = kvh * C.R + n % C.R;
-  for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
-    float o = 0.0f;
-    for (int p = 0; p < nparts; ++p) {
-      const float lp = P.ws_lse[(slot0 + p) * NCOL + col];
-      const float w = (M == kNegInf) ? 0.0f : exp2f(lp - M);
-      o += w * P.ws_o[((slot0 + p) * NCOL + col) * D + dd];
-    }
-    emit_value(C, b, h, qi, dd, o * invW);
-  }
-  if (threadIdx.x == 0) emit_lse(C, b, h, qi, W > 0.0f ? M + log2f(W) : kNegInf);
-}
-
 struct LseParams {
   const float *po;
   const float *pl;
@@ -860,8 +907,7 @@ static bool fast_eligible(const kv4_tensor *q, const kv4_tensor *kp, const kv4_t
   const int64_t ng = S.d / S.G;
   const int ss = dtype_size(ks->dtype);
   for (const kv4_tensor *t : {kp, vp}) {
-    if (!aligned16(t->data) || t->stride[3] != 1 || t->stride[2] % 16 || t->shape[3] % 16)
-      return false;
+    if (!aligned16(t->data) || t->stride[3] != 1 || t->stride[2] % 16) return false;
     if (t->shape[1] > 1 && t->stride[1] % 16) return false;
     if (t->shape[0] > 1 && t->stride[0] % 16) return false;
   }
@@ -947,7 +993,8 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     pl.ctas = static_cast<int>((pl.total_tiles + L - 1) / L);
     pl.maxp = static_cast<int>((pl.tpu - 1 + L - 1) / L + 1);
     pl.need_merge = (L % pl.tpu) != 0;
-    pl.ws_bytes = pl.need_merge ? static_cast<size_t>(pl.units) * pl.maxp * NCOL *
+    pl.ws_bytes = pl.need_merge ? (static_cast<size_t>(pl.units) * sizeof(int) + 15) / 16 * 16 +
+                                      static_cast<size_t>(pl.units) * pl.maxp * NCOL *
                                       (static_cast<size_t>(pl.D) + 1) * sizeof(float)
                                 : 0;
   } else {
@@ -958,24 +1005,26 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
   }
 }
 
-// Packed K/V map: 5-D view {16 B, token, 16-B chunk, head, batch} so that a
-// box lands in shared memory chunk-major ([chunk][token][16 B]).
-static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int nch, int tokens) {
+// Packed K/V map: 4-D {row bytes, token, head, batch}, box {P, TOK, 1, 1},
+// swizzled by the row width (32/64/128 B) so fragment loads are bank-conflict free.
+static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int row_bytes, int tokens) {
   auto enc = get_encode();
   const int64_t sh = t->shape[1] > 1 ? t->stride[1] : t->stride[2] * t->shape[2];
   const int64_t sb = t->shape[0] > 1 ? t->stride[0] : sh * t->shape[1];
-  cuuint64_t dims[5] = {16, static_cast<cuuint64_t>(t->shape[2]),
-                        static_cast<cuuint64_t>(t->shape[3] / 16),
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t->shape[3]), static_cast<cuuint64_t>(t->shape[2]),
                         static_cast<cuuint64_t>(t->shape[1]),
                         static_cast<cuuint64_t>(t->shape[0])};
-  cuuint64_t strides[4] = {static_cast<cuuint64_t>(t->stride[2]), 16,
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t->stride[2]),
                            static_cast<cuuint64_t>((sh + 15) / 16 * 16),
                            static_cast<cuuint64_t>((sb + 15) / 16 * 16)};
-  cuuint32_t box[5] = {16, static_cast<cuuint32_t>(tokens), static_cast<cuuint32_t>(nch), 1, 1};
-  cuuint32_t es[5] = {1, 1, 1, 1, 1};
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, t->data, dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(row_bytes), static_cast<cuuint32_t>(tokens), 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUtensorMapSwizzle sw = row_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                          : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, t->data, dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
 }
 
@@ -1007,19 +1056,14 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
   using Cfg = FastCfg<D, G, ST>;
   CUtensorMap tkp, tvp, tks, tvs;
   int rc;
-  if ((rc = encode_packed(&tkp, kp, Cfg::NCH, TOK))) return rc;
-  if ((rc = encode_packed(&tvp, vp, Cfg::NCH, TOK))) return rc;
+  if ((rc = encode_packed(&tkp, kp, Cfg::P, TOK))) return rc;
+  if ((rc = encode_packed(&tvp, vp, Cfg::P, TOK))) return rc;
   if ((rc = encode_scales(&tks, ks, Cfg::TS))) return rc;
   if ((rc = encode_scales(&tvs, vs, Cfg::TS))) return rc;
   occupancy_of<D, G, ST, SPLIT>();  // sets the smem attribute once
   kv4_attn_fast<D, G, ST, SPLIT><<<pl.ctas, 128, Cfg::SMEM, st>>>(FP, tkp, tvp, tks, tvs);
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
-  if (pl.need_merge) {
-    dim3 grid(pl.units, NCOL);
-    kv4_merge_slots<<<grid, 128, 0, st>>>(FP);
-    rc = cuda_status(cudaGetLastError());
-  }
   return rc;
 }
 
@@ -1104,7 +1148,13 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
     FP.L = pl.L;
     FP.total_tiles = pl.total_tiles;
     FP.maxp = pl.maxp;
+    // workspace: partial o, then lse from the front; the per-unit counters
+    // (zero between calls) are the LAST units*4 bytes of the caller's buffer.
     FP.ws_o = static_cast<float *>(ws);
+    FP.counters = pl.ws_bytes ? reinterpret_cast<int *>(
+                                    static_cast<char *>(ws) +
+                                    ((ws_bytes - static_cast<size_t>(pl.units) * 4) & ~size_t(3)))
+                              : nullptr;
     FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) * pl.maxp * NCOL * pl.D
                             : nullptr;
     if (pl.sdt == KV4_BF16) return launch_fast_st<__nv_bfloat16>(FP, pl, kp, ks, vp, vs, st);
@@ -1179,7 +1229,7 @@ extern "C" int kv4_attention_plan(const kv4_tensor *q, const kv4_tensor *k_packe
   plan->tiles_per_cta = pl.L;
   plan->units = pl.units;
   plan->max_parts = pl.maxp;
-  plan->kernels = pl.need_merge ? 2 : 1;
+  plan->kernels = 1;
   plan->workspace_bytes = static_cast<int64_t>(pl.ws_bytes);
   return KV4_OK;
 }

@@ -69,17 +69,31 @@ def dequantize_into(packed: torch.Tensor, scales: torch.Tensor, out: torch.Tenso
 # attention
 # --------------------------------------------------------------------------
 _WS: dict = {}
+_COUNTER_RESERVE = 1 << 16  # zeroed tail of every workspace: room for 16384 units' counters
 
 
-def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor | None:
-    """Per (device, stream) scratch buffer for split-sequence partials."""
+def _workspace(dev: torch.device, plan: AttnPlan) -> torch.Tensor | None:
+    """Per (device, stream) scratch buffer for split-sequence partials.
+
+    Layout: partial data from the front (never past ``numel - reserve``), a
+    zero-initialised tail of ``reserve`` bytes whose end holds the kernel's
+    per-unit counters.  The kernel returns the counters to zero, and no call
+    writes data into the tail, so the tail stays zero between calls."""
+    nbytes = int(plan.workspace_bytes)
     if nbytes <= 0:
         return None
+    counters = (int(plan.units) * 4 + 15) // 16 * 16
+    data = nbytes - counters
+    reserve = max(_COUNTER_RESERVE, counters)
     key = (dev.index, _stream(dev))
-    buf = _WS.get(key)
-    if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
-        _WS[key] = buf
+    buf, res = _WS.get(key, (None, 0))
+    if buf is None or res < reserve or buf.numel() - res < data:
+        res = max(res, reserve)
+        size = max(data, 1 << 20) + res
+        if buf is not None:
+            size = max(size, buf.numel())
+        buf = torch.zeros(size, dtype=torch.uint8, device=dev)
+        _WS[key] = (buf, res)
     return buf
 
 
@@ -114,7 +128,7 @@ def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = Fa
     check("kv4_attention_plan",
           L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
                                optr, ctypes.byref(p)))
-    ws = _workspace(q.device, int(p.workspace_bytes))
+    ws = _workspace(q.device, p)
     check("kv4_attention",
           L.kv4_attention(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
                           float(sm_scale), ws.data_ptr() if ws is not None else None,
@@ -133,7 +147,7 @@ def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, s
     check("kv4_attention_plan",
           L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
                                optr, ctypes.byref(p)))
-    ws = _workspace(q.device, int(p.workspace_bytes))
+    ws = _workspace(q.device, p)
     check("kv4_attention_partial",
           L.kv4_attention_partial(*[ctypes.byref(d) for d in ds], ctypes.byref(dl),
                                   int(k_offset), int(sk_total), int(group_size), int(is_causal),
