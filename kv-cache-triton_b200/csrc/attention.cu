@@ -193,6 +193,8 @@ struct FastParams {
   float *ws_o;    // [units*maxp][NCOL][d]
   float *ws_lse;  // [units*maxp][NCOL]   (log2 domain)
   int *counters;  // [units] finished-segment counts (zero between calls)
+  const char *ks, *vs;         // scale tensors
+  int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
 };
 
 // Shared-memory layout of one stage (per tensor): packed codes token-major
@@ -211,12 +213,11 @@ struct FastCfg {
   static constexpr int SH = (P == 32) ? 2 : (P == 64) ? 1 : 0;    // row -> key shift
   static constexpr int KP = TOK * P;          // packed bytes per stage per tensor
   static constexpr int KS = TOK * SROW;       // scale bytes per stage per tensor
-  static constexpr int TS = (TOK * NG <= 256) ? TOK : 256 / NG;  // tokens per scale TMA box
-  static constexpr int NSB = TOK / TS;        // scale boxes per stage per tensor
   static constexpr int STAGE = ((2 * KP + 2 * KS) + 1023) / 1024 * 1024;
-  static constexpr int STAGES = (D == 256) ? 2 : 3;
+  static constexpr int STAGES = 2;  // 2 x 18 KB (d=128) keeps 4 CTAs/SM resident
   static constexpr int MERGE = NWARP * NCOL * D * 4;
-  static constexpr int SMEM = STAGES * STAGE + MERGE + 3 * NWARP * NCOL * 4 + 2 * NCOL * 4 +
+  static_assert(MERGE <= STAGES * STAGE, "merge buffer aliases the stages");
+  static constexpr int SMEM = STAGES * STAGE + 3 * NWARP * NCOL * 4 + 2 * NCOL * 4 +
                               16 * STAGES + 1024;
   static constexpr uint32_t TX = 2 * KP + 2 * KS;
 };
@@ -284,11 +285,9 @@ __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
 }
 
 template <int D, int G, typename ST, bool SPLIT>
-__global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
+__global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
-                  const __grid_constant__ CUtensorMap tm_vp,
-                  const __grid_constant__ CUtensorMap tm_ks,
-                  const __grid_constant__ CUtensorMap tm_vs) {
+                  const __grid_constant__ CUtensorMap tm_vp) {
   using Cfg = FastCfg<D, G, ST>;
   constexpr int NCH = Cfg::NCH, NG = Cfg::NG, CPG = Cfg::CPG;
   const AttnCommon &C = P.c;
@@ -296,8 +295,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  float *merge_o = reinterpret_cast<float *>(smem + Cfg::STAGES * Cfg::STAGE);
-  float *merge_m = merge_o + NWARP * NCOL * D;
+  // the warp-merge buffer aliases the stage buffers: each CTA flushes once,
+  // after its last tile, when no TMA load is in flight any more
+  float *merge_o = reinterpret_cast<float *>(smem);
+  float *merge_m = reinterpret_cast<float *>(smem + Cfg::STAGES * Cfg::STAGE);
   float *merge_l = merge_m + NWARP * NCOL;
   float *merge_f = merge_l + NWARP * NCOL;
   float *merge_lse = merge_f + NWARP * NCOL;
@@ -309,10 +310,17 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   const int lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tg = lane & 3;
 
-  const int first_tile = static_cast<int>(blockIdx.x) * P.L;  // total tiles < 2^31 (host check)
-  const int last_tile = min(first_tile + P.L, static_cast<int>(P.total_tiles));  // exclusive
-  const int ntiles = last_tile - first_tile;
+  // Split-K: CTA = (unit, part); part p of kparts streams tiles
+  // [p*tpu/kparts, (p+1)*tpu/kparts) of its unit's sequence.
+  const int kparts = P.maxp;
+  const int u = static_cast<int>(blockIdx.x) / kparts;
+  const int part = static_cast<int>(blockIdx.x) - u * kparts;
+  const int t_begin = static_cast<int>(static_cast<int64_t>(part) * P.tpu / kparts);
+  const int t_end = static_cast<int>(static_cast<int64_t>(part + 1) * P.tpu / kparts);
+  const int ntiles = t_end - t_begin;
   if (ntiles <= 0) return;
+  const int u_bk = u / P.hc, u_hc = u - u_bk * P.hc;
+  const int u_b = u_bk / C.Hkv, u_kvh = u_bk - u_b * C.Hkv;
 
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
@@ -321,8 +329,6 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     sh_abort = 0;
     prefetch_tmap(&tm_kp);
     prefetch_tmap(&tm_vp);
-    prefetch_tmap(&tm_ks);
-    prefetch_tmap(&tm_vs);
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(bar_base + 8 * s, 1);                            // full: producer + tx
       mbar_init(bar_base + 8 * (Cfg::STAGES + s), NWARP);        // empty: one per warp
@@ -331,39 +337,22 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   }
   __syncthreads();
 
-  // Tile bookkeeping is incremental: the (unit, tile-in-unit) of the first
-  // tile costs one division; afterwards both the consumer position and the
-  // producer's (STAGES ahead) advance by +1 with a wrap at tpu.
-  const int u_first = first_tile / P.tpu;
-  const int ti_first = first_tile - u_first * P.tpu;
-  int iss_u = u_first, iss_ti = ti_first, iss_b = 0, iss_kvh = 0, iss_bu = -1;
-
-  auto issue = [&](int i) {  // next tile in order -> stage i % STAGES (thread 0 only)
-    if (iss_u != iss_bu) {
-      const int bk = iss_u / P.hc;
-      iss_b = bk / C.Hkv;
-      iss_kvh = bk - iss_b * C.Hkv;
-      iss_bu = iss_u;
-    }
-    const int b = iss_b, kvh = iss_kvh;
-    const int t0 = iss_ti * TOK;
-    if (++iss_ti == P.tpu) {
-      iss_ti = 0;
-      ++iss_u;
-    }
+  auto issue = [&](int i) {  // local tile i -> stage i % STAGES (thread 0 only)
+    const int b = u_b, kvh = u_kvh;
+    const int t0 = (t_begin + i) * TOK;
     const int s = i % Cfg::STAGES;
     const uint32_t bar = bar_base + 8 * s;
     const uint32_t dst = smem_base + s * Cfg::STAGE;
-    mbar_arrive_expect_tx(bar, Cfg::TX);
+    // packed codes: 2 tiled TMA loads (zero-filled past sk); scales: one bulk
+    // copy per tensor of the tile's contiguous rows, rounded up to 16 bytes
+    const int rem = min(TOK, C.sk - t0);
+    const uint32_t sbytes = static_cast<uint32_t>(rem * Cfg::SROW + 15) & ~15u;
+    mbar_arrive_expect_tx(bar, 2 * Cfg::KP + 2 * sbytes);
     tma_load_4d(dst, &tm_kp, bar, 0, t0, kvh, b);
     tma_load_4d(dst + Cfg::KP, &tm_vp, bar, 0, t0, kvh, b);
-#pragma unroll
-    for (int k = 0; k < Cfg::NSB; ++k) {
-      const int x = (t0 + k * Cfg::TS) * NG;
-      tma_load_3d(dst + 2 * Cfg::KP + k * Cfg::TS * Cfg::SROW, &tm_ks, bar, x, kvh, b);
-      tma_load_3d(dst + 2 * Cfg::KP + Cfg::KS + k * Cfg::TS * Cfg::SROW, &tm_vs, bar, x, kvh,
-                  b);
-    }
+    const int64_t soff = static_cast<int64_t>(t0) * Cfg::SROW;
+    bulk_load(dst + 2 * Cfg::KP, P.ks + b * P.ks_sb + kvh * P.ks_sh + soff, sbytes, bar);
+    bulk_load(dst + 2 * Cfg::KP + Cfg::KS, P.vs + b * P.vs_sb + kvh * P.vs_sh + soff, sbytes, bar);
   };
 
   if (tid == 0) {
@@ -378,13 +367,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   float o_acc[NCH][2][4];               // O^T fragments [chunk][j][c]
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
-  int cur_unit = -1;
   int col_lim[2];
   int lim_min = 0;  // smallest key limit over the CTA's columns (warp-uniform)
 
-  auto load_unit = [&](int u) {
-    const int bk = u / P.hc, hcid = u % P.hc;
-    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+  auto load_unit = [&]() {
+    const int hcid = u_hc, b = u_b, kvh = u_kvh;
     {
       // B operand column n = g
       const int n = hcid * NCOL + g;
@@ -399,10 +386,23 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         float v[8], hi[8], lo[8];
+        const int64_t qoff = qbase + (32 * c + 8 * tg) * C.qs[3];
+        if (ok && C.q_dtype == KV4_BF16 && C.qs[3] == 1 &&
+            (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(C.q) + qoff) & 15) == 0) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(C.q) + qoff);
+          const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            v[2 * e] = bf16lo_to_f32(ws4[e]);
+            v[2 * e + 1] = bf16hi_to_f32(ws4[e]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            v[e] = ok ? load_as_f32(C.q, C.q_dtype, qbase + (32 * c + 8 * tg + e) * C.qs[3]) : 0.0f;
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int dd = 32 * c + 8 * tg + e;
-          v[e] = ok ? load_as_f32(C.q, C.q_dtype, qbase + dd * C.qs[3]) : 0.0f;
           hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
           lo[e] = SPLIT ? __bfloat162float(__float2bfloat16_rn(v[e] - hi[e])) : 0.0f;
           gsum[c / CPG] += hi[e] + lo[e];
@@ -465,9 +465,9 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   // either write the output (unit wholly inside this CTA) or write a partial
   // slot; the last CTA to finish a split unit (per-unit counter) merges all
   // of the unit's slots and writes the output, then re-arms the counter.
-  auto flush = [&](int u) {
-    const int bk = u / P.hc, hcid = u % P.hc;
-    const int b = bk / C.Hkv, kvh = bk % C.Hkv;
+  auto flush = [&]() {
+    const int hcid = u_hc, b = u_b, kvh = u_kvh;
+    __syncthreads();  // merge_o aliases the stages other warps may still be reading
 #pragma unroll
     for (int j = 0; j < 2; ++j) {  // l over the 8 token-row lanes
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
@@ -498,11 +498,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
     }
     __syncthreads();
-    const int ft = u * P.tpu;
-    const int first_cta = ft / P.L;
-    const int last_cta = (ft + P.tpu - 1) / P.L;
-    const bool whole = first_cta == last_cta;
-    const int slot = u * P.maxp + (static_cast<int>(blockIdx.x) - first_cta);
+    const bool whole = kparts == 1;
+    const int slot = u * kparts + part;
     if (tid < NCOL) {  // per-column warp weights (already divided by the total l)
       float M = kNegInf;
 #pragma unroll
@@ -536,43 +533,68 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
     }
     if (!whole) {
-      __threadfence();
+      // Bar.sync orders every thread's partial stores before thread 0's
+      // acq_rel atomic (release is cumulative); the last CTA to arrive
+      // acquires them all and merges the unit's kparts slots.
       __syncthreads();
       if (tid == 0) {
-        const int nparts = last_cta - first_cta + 1;
-        const int prev = atomicAdd(&P.counters[u], 1);
-        sh_last = (prev == nparts - 1);
+        const int prev = atom_add_acq_rel_gpu(&P.counters[u], 1);
+        sh_last = (prev == kparts - 1);
         if (sh_last) P.counters[u] = 0;  // re-arm for the next call
       }
       __syncthreads();
       if (sh_last) {
-        __threadfence();
-        const int nparts = last_cta - first_cta + 1;
-        const int64_t slot0 = static_cast<int64_t>(u) * P.maxp;
+        const int nparts = kparts;
+        const int64_t slot0 = static_cast<int64_t>(u) * kparts;
+        float *wts = reinterpret_cast<float *>(smem);  // stage buffers are idle now
+        for (int k = tid; k < nparts * NCOL; k += blockDim.x)
+          wts[k] = __ldcg(&P.ws_lse[slot0 * NCOL + k]);
+        __syncthreads();
         if (tid < NCOL) {
           float M = kNegInf;
-          for (int p = 0; p < nparts; ++p) M = fmaxf(M, __ldcg(&P.ws_lse[(slot0 + p) * NCOL + tid]));
+          for (int p = 0; p < nparts; ++p) M = fmaxf(M, wts[p * NCOL + tid]);
           float W = 0.0f;
-          for (int p = 0; p < nparts; ++p)
-            W += (M == kNegInf) ? 0.0f : exp2f(__ldcg(&P.ws_lse[(slot0 + p) * NCOL + tid]) - M);
-          merge_m[tid] = M;
-          merge_l[tid] = W > 0.0f ? 1.0f / W : 0.0f;
+          for (int p = 0; p < nparts; ++p) {
+            const float w = (M == kNegInf) ? 0.0f : exp2f(wts[p * NCOL + tid] - M);
+            wts[p * NCOL + tid] = w;
+            W += w;
+          }
+          const float inv = W > 0.0f ? 1.0f / W : 0.0f;
+          for (int p = 0; p < nparts; ++p) wts[p * NCOL + tid] *= inv;
           merge_lse[tid] = W > 0.0f ? M + log2f(W) : kNegInf;
         }
         __syncthreads();
-        for (int idx = tid; idx < NCOL * D; idx += blockDim.x) {
-          const int col = idx / D, dd = idx % D;
+        constexpr int D4 = D / 4;
+        for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
+          const int col = idx / D4, d4 = idx % D4;
           const int n = hcid * NCOL + col;
           if (n >= P.ncols) continue;
-          const float M = merge_m[col];
-          float o = 0.0f;
-          if (M != kNegInf)
-            for (int p = 0; p < nparts; ++p) {
-              const float w = exp2f(__ldcg(&P.ws_lse[(slot0 + p) * NCOL + col]) - M);
-              o += w * __ldcg(&P.ws_o[((slot0 + p) * NCOL + col) * D + dd]);
+          const float4 *src =
+              reinterpret_cast<const float4 *>(P.ws_o + (slot0 * NCOL + col) * D) + d4;
+          const int pstride = NCOL * D4;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          int p = 0;
+          for (; p + 4 <= nparts; p += 4) {  // four loads in flight per step
+            float4 v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = __ldcg(src + (p + e) * pstride);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float w = wts[(p + e) * NCOL + col];
+              acc.x += w * v[e].x; acc.y += w * v[e].y; acc.z += w * v[e].z; acc.w += w * v[e].w;
             }
+          }
+          for (; p < nparts; ++p) {
+            const float4 v = __ldcg(src + p * pstride);
+            const float w = wts[p * NCOL + col];
+            acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+          }
           const int qi = n / C.R, h = kvh * C.R + n % C.R;
-          emit_value(C, b, h, qi, dd, o * merge_l[col]);
+          const int dd = 4 * d4;
+          emit_value(C, b, h, qi, dd, acc.x);
+          emit_value(C, b, h, qi, dd + 1, acc.y);
+          emit_value(C, b, h, qi, dd + 2, acc.z);
+          emit_value(C, b, h, qi, dd + 3, acc.w);
           if (dd == 0) emit_lse(C, b, h, qi, merge_lse[col]);
         }
       }
@@ -596,20 +618,13 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   }
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
-  int u = u_first, ti = ti_first - 1;
+  load_unit();  // q loads overlap the first TMA loads already in flight
   int stage = -1;
   uint32_t phase = 1;
   for (int i = 0; i < ntiles; ++i) {
-    if (++ti == P.tpu) {
-      ti = 0;
-      ++u;
-    }
+    const int ti = t_begin + i;
     if (++stage == Cfg::STAGES) stage = 0;
     if (stage == 0) phase ^= 1u;
-    if (u != cur_unit) {
-      load_unit(u);
-      cur_unit = u;
-    }
     if (!*reinterpret_cast<volatile int *>(&sh_abort) &&
         !mbar_wait_bounded(bar_base + 8 * stage, phase)) {
       atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
@@ -622,16 +637,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     const int tok0 = ti * TOK + WROWS * warp;  // first token row of this warp
 
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
-    float sc[2][NG][4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int gi = 0; gi < NG; ++gi) {
-        sc[h][gi][0] = bias[gi][0];
-        sc[h][gi][1] = bias[gi][1];
-        sc[h][gi][2] = bias[gi][0];
-        sc[h][gi][3] = bias[gi][1];
-      }
+    float sc[2][NG][4];  // first MMA of each group takes the bias as its C input
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int gi = c / CPG;
@@ -641,7 +647,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
         const uint32_t x0 = lds32(base), x1 = lds32(base + 8 * P_);
         const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
         const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
-        mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
+        if (c % CPG == 0)
+          mma_bf16_16816_c(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
+                           bias[gi][1], bias[gi][0], bias[gi][1]);
+        else
+          mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
         mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
         if constexpr (SPLIT) {
           mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
@@ -676,6 +686,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
           const int t = tok0 + 16 * h + 8 * r + g;
           if (t >= col_lim[0]) s[h][r][0] = kNegInf;
           if (t >= col_lim[1]) s[h][r][1] = kNegInf;
+          if (t >= C.sk) {  // rows past the cache hold stale smem: keep P * scale finite
+#pragma unroll
+            for (int gi = 0; gi < NG; ++gi) vsc[h][r][gi] = 0.0f;
+          }
         }
     }
     // ---------------- online softmax over 32 rows (lazy rescale) --------
@@ -786,9 +800,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
       issue(i + Cfg::STAGES);
     }
-    const bool unit_end = (ti == P.tpu - 1) || (i == ntiles - 1);
-    if (unit_end) flush(u);
   }
+  flush();
   if (sh_abort && tid == 0) {
     // drain: wait (bounded) for the loads this CTA may still have in flight
     for (int i = max(0, ntiles - Cfg::STAGES); i < ntiles; ++i) {
@@ -986,13 +999,14 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     const int occ = fast_occupancy(pl.D, S.G, pl.sdt, pl.split);
     int64_t target = static_cast<int64_t>(sm_count()) * occ;
     if (opts && opts->max_ctas > 0) target = std::min<int64_t>(target, opts->max_ctas);
-    int64_t L = (pl.total_tiles + target - 1) / target;
-    if (L < 2) L = 2;
-    if (opts && opts->tiles_per_cta > 0) L = opts->tiles_per_cta;
-    pl.L = static_cast<int>(L);
-    pl.ctas = static_cast<int>((pl.total_tiles + L - 1) / L);
-    pl.maxp = static_cast<int>((pl.tpu - 1 + L - 1) / L + 1);
-    pl.need_merge = (L % pl.tpu) != 0;
+    // split-K: kparts CTAs per unit, as many as fit one wave of resident CTAs
+    int64_t k = std::max<int64_t>(1, target / pl.units);
+    if (opts && opts->tiles_per_cta > 0) k = (pl.tpu + opts->tiles_per_cta - 1) / opts->tiles_per_cta;
+    k = std::min<int64_t>(k, pl.tpu);
+    pl.maxp = static_cast<int>(k);
+    pl.L = static_cast<int>((pl.tpu + k - 1) / k);
+    pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
+    pl.need_merge = k > 1;
     pl.ws_bytes = pl.need_merge ? (static_cast<size_t>(pl.units) * sizeof(int) + 15) / 16 * 16 +
                                       static_cast<size_t>(pl.units) * pl.maxp * NCOL *
                                       (static_cast<size_t>(pl.D) + 1) * sizeof(float)
@@ -1028,40 +1042,18 @@ static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int row_bytes, in
   return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
 }
 
-static int encode_scales(CUtensorMap *tm, const kv4_tensor *t, int tokens_per_box) {
-  auto enc = get_encode();
-  const int ss = dtype_size(t->dtype);
-  const int64_t ng = t->shape[3];
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(t->shape[2] * ng),
-                        static_cast<cuuint64_t>(t->shape[1]),
-                        static_cast<cuuint64_t>(t->shape[0])};
-  int64_t s1 = t->shape[1] > 1 ? t->stride[1] : t->shape[2] * ng;
-  int64_t s0 = t->shape[0] > 1 ? t->stride[0] : s1 * t->shape[1];
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>((s1 * ss + 15) / 16 * 16),
-                           static_cast<cuuint64_t>((s0 * ss + 15) / 16 * 16)};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(tokens_per_box * ng), 1, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUtensorMapDataType dt =
-      ss == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-  CUresult r = enc(tm, dt, 3, t->data, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? KV4_OK : KV4_ERR_LAYOUT;
-}
 
 template <int D, int G, typename ST, bool SPLIT>
 static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
                          cudaStream_t st) {
   using Cfg = FastCfg<D, G, ST>;
-  CUtensorMap tkp, tvp, tks, tvs;
+  CUtensorMap tkp, tvp;
   int rc;
   if ((rc = encode_packed(&tkp, kp, Cfg::P, TOK))) return rc;
   if ((rc = encode_packed(&tvp, vp, Cfg::P, TOK))) return rc;
-  if ((rc = encode_scales(&tks, ks, Cfg::TS))) return rc;
-  if ((rc = encode_scales(&tvs, vs, Cfg::TS))) return rc;
   occupancy_of<D, G, ST, SPLIT>();  // sets the smem attribute once
-  kv4_attn_fast<D, G, ST, SPLIT><<<pl.ctas, 128, Cfg::SMEM, st>>>(FP, tkp, tvp, tks, tvs);
+  kv4_attn_fast<D, G, ST, SPLIT><<<pl.ctas, 128, Cfg::SMEM, st>>>(FP, tkp, tvp);
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
   return rc;
@@ -1148,6 +1140,15 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
     FP.L = pl.L;
     FP.total_tiles = pl.total_tiles;
     FP.maxp = pl.maxp;
+    {
+      const int ss = dtype_size(ks->dtype);
+      FP.ks = static_cast<const char *>(ks->data);
+      FP.vs = static_cast<const char *>(vs->data);
+      FP.ks_sb = ks->stride[0] * ss;
+      FP.ks_sh = ks->stride[1] * ss;
+      FP.vs_sb = vs->stride[0] * ss;
+      FP.vs_sh = vs->stride[1] * ss;
+    }
     // workspace: partial o, then lse from the front; the per-unit counters
     // (zero between calls) are the LAST units*4 bytes of the caller's buffer.
     FP.ws_o = static_cast<float *>(ws);
