@@ -48,7 +48,8 @@ enum {
   KV4_ERR_WORKSPACE = 5,   /* workspace missing or too small */
   KV4_ERR_CUDA = 6,        /* a CUDA runtime call failed (see kv4_last_cuda_error) */
   KV4_ERR_UNSUPPORTED = 7, /* valid request outside what the library implements */
-  KV4_ERR_DEVICE = 8       /* a kernel reported a device-side error (bounded wait expired) */
+  KV4_ERR_DEVICE = 8,      /* a kernel reported a device-side error (bounded wait expired) */
+  KV4_ERR_SCRATCH_LIMIT = 9 /* kv4_attention_noalloc: request exceeds its fixed scratch area */
 };
 
 typedef struct kv4_tensor {
@@ -169,6 +170,24 @@ int kv4_attention_partial(const kv4_tensor *q, const kv4_tensor *k_packed,
  */
 int kv4_lse_combine(const float *parts_o, const float *parts_lse, int64_t n_parts,
                     const kv4_tensor *out, void *stream);
+
+/*
+ * kv4_attention without a workspace argument, for callers that cannot
+ * allocate device memory at the call site (no allocator reachable from
+ * their runtime, or a serving step that must not touch the allocator).  It
+ * has no counterpart in the reference.  Same arguments and results as
+ * kv4_attention; the split-sequence partials go to a scratch area of
+ * 4 MiB compiled into the library (each GPU that loads the library keeps it
+ * until exit; at most 16384 work units and 4 MiB - 64 KiB of partials,
+ * otherwise KV4_ERR_SCRATCH_LIMIT).  Nothing is allocated.  The first call on
+ * a device looks up the area's device address (make that first call before
+ * any stream capture).  All calls share the area: calls that overlap on the
+ * GPU race and must be serialised by the caller.
+ */
+int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_packed,
+                          const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                          const kv4_tensor *v_scales, const kv4_tensor *out, int group_size,
+                          int is_causal, float sm_scale, void *stream);
 
 /* Read-and-clear the device error word that bounded waits set (synchronizes the stream). */
 int kv4_device_error(void *stream, int *flag_out);

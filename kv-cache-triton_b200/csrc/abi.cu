@@ -36,6 +36,8 @@ extern "C" const char *kv4_strerror(int status) {
     case KV4_ERR_CUDA: return "CUDA runtime error";
     case KV4_ERR_UNSUPPORTED: return "unsupported configuration";
     case KV4_ERR_DEVICE: return "device-side error (bounded wait expired)";
+    case KV4_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than kv4_attention_noalloc's fixed 4 MiB area";
     default: return "unknown status";
   }
 }

@@ -1269,3 +1269,75 @@ extern "C" int kv4_device_error(void *stream, int *flag_out) {
   *flag_out = v;
   return rc;
 }
+
+// ===========================================================================
+// Allocation-free variant of kv4_attention
+// ===========================================================================
+// Some callers cannot allocate device memory when they call us: code running
+// inside a memory-pool-less runtime or an embedding host whose allocator is
+// not reachable from this call site, or a step that must not touch the
+// device allocator while it is recording or serving.  For them,
+// kv4_attention_noalloc uses a fixed scratch area compiled into this
+// library instead of a caller-provided workspace.  Every GPU that loads the
+// library holds this array until the process exits.
+namespace kv4 {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;   // 4 MiB in total
+constexpr size_t kNoAllocCounterBytes = size_t(64) << 10;  // tail: up to 16384 work units
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's name is only a host-side stand-in in host code; the device
+// address is looked up once per device, with that device current.
+static void *noalloc_scratch_ptr(int dev, int *status) {
+  static std::mutex mu;
+  static void *ptrs[64] = {};
+  if (dev < 0 || dev >= 64) {
+    *status = KV4_ERR_UNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *status = cuda_status(e);
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *status = KV4_OK;
+  return ptrs[dev];
+}
+
+}  // namespace kv4
+
+extern "C" int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_packed,
+                                     const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                                     const kv4_tensor *v_scales, const kv4_tensor *out,
+                                     int group_size, int is_causal, float sm_scale,
+                                     void *stream) {
+  kv4_attn_plan plan;
+  int rc = kv4_attention_plan(q, k_packed, k_scales, v_packed, v_scales, out, group_size,
+                              is_causal, nullptr, &plan);
+  if (rc) return rc;
+  if (plan.workspace_bytes == 0)  // nothing to scratch: identical to kv4_attention
+    return kv4_attention(q, k_packed, k_scales, v_packed, v_scales, out, group_size, is_causal,
+                         sm_scale, nullptr, 0, nullptr, stream);
+  const size_t counters = static_cast<size_t>(plan.units) * 4;
+  const size_t data = static_cast<size_t>(plan.workspace_bytes) - ((counters + 15) / 16 * 16);
+  if (counters > kNoAllocCounterBytes || data > kNoAllocScratchBytes - kNoAllocCounterBytes)
+    return KV4_ERR_SCRATCH_LIMIT;
+  int dev = 0;
+  rc = cuda_status(cudaGetDevice(&dev));
+  if (rc) return rc;
+  void *scratch = noalloc_scratch_ptr(dev, &rc);
+  if (rc) return rc;
+  // The counters (the last `counters` bytes of the area) must start at zero;
+  // clear them on this stream in case an earlier call did not complete.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = cuda_status(cudaMemsetAsync(static_cast<char *>(scratch) + kNoAllocScratchBytes - counters,
+                                   0, counters, st));
+  if (rc) return rc;
+  return kv4_attention(q, k_packed, k_scales, v_packed, v_scales, out, group_size, is_causal,
+                       sm_scale, scratch, kNoAllocScratchBytes, nullptr, stream);
+}

@@ -19,12 +19,13 @@ TIE_HALF_AWAY, TIE_HALF_EVEN = 0, 1
 KV4_OK = 0
 KV4_ERR_INVALID, KV4_ERR_DTYPE, KV4_ERR_SHAPE, KV4_ERR_LAYOUT = 1, 2, 3, 4
 KV4_ERR_WORKSPACE, KV4_ERR_CUDA, KV4_ERR_UNSUPPORTED, KV4_ERR_DEVICE = 5, 6, 7, 8
+KV4_ERR_SCRATCH_LIMIT = 9
 
 # every function the header declares, for load checks
 EXPORTED = (
     "kv4_version", "kv4_strerror", "kv4_last_cuda_error", "kv4_quantize", "kv4_append_kv",
     "kv4_dequantize", "kv4_attention", "kv4_attention_plan", "kv4_attention_partial",
-    "kv4_lse_combine", "kv4_device_error",
+    "kv4_lse_combine", "kv4_device_error", "kv4_attention_noalloc",
 )
 
 
@@ -97,6 +98,7 @@ def lib() -> ctypes.CDLL:
                                         P(AttnOpts), vp]
     L.kv4_lse_combine.argtypes = [vp, vp, i64, T, vp]
     L.kv4_device_error.argtypes = [vp, P(ctypes.c_int)]
+    L.kv4_attention_noalloc.argtypes = [T, T, T, T, T, T, i32, i32, f32, vp]
     for name in EXPORTED:
         if name not in ("kv4_version", "kv4_strerror", "kv4_last_cuda_error"):
             getattr(L, name).restype = i32
