@@ -60,6 +60,19 @@ def _dist():
     return ws, rank, local
 
 
+def _traffic():
+    """DRAM bytes per launch of the attention kernel from the committed ncu
+    summary (profiles/kv4_attn_fast_config2.md), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "kv4_attn_fast_config2.md")) as f:
+            for line in f:
+                if line.startswith("| traffic_bytes_per_launch |"):
+                    return int(line.split("|")[2])
+    except Exception:
+        pass
+    return None
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -284,10 +297,10 @@ def run_ours(args, ws, rank, local):
         "e2e": {"value": round(ws * STEP_BYTES * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast (+kv4_merge_slots)",
+        "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": None},
+                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": _traffic()},
         "clocks": clk.summary(),
         "plan": {"path": int(p.path), "ctas": int(p.ctas), "tiles_per_cta": int(p.tiles_per_cta),
                  "kernels_per_attention": int(p.kernels)},
