@@ -603,18 +603,18 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   };
 
   const uint32_t ones = 0x3F803F80u;  // bf16x2 (1, 1)
-  // Lane-constant smem offsets inside a stage.  K rows 32w+16h+g (+8) share
-  // the swizzle key of row g; V rows 32w+16h+2tg (+1, +8, +9) that of row 2tg.
+  // Lane-constant ldmatrix row addresses inside a stage: lane L feeds row
+  // r = 8*((L>>3)&1) + (L&7) of the warp's 16-row sub-tile, 16-byte chunk
+  // c + (L>>4), with the TMA swizzle applied (the key of a row does not change
+  // by +16 rows, so one offset per chunk pair serves both sub-tiles).
   constexpr int P_ = Cfg::P;
-  const int kkey = ((WROWS * warp + g) >> Cfg::SH) & Cfg::SWZ;
-  // (with 128-byte rows the odd V rows 2tg+1, 2tg+9 carry key ^ 1)
-  const int vkey = ((WROWS * warp + 2 * tg) >> Cfg::SH) & Cfg::SWZ;
-  constexpr int VODD = (Cfg::SH == 0) ? 1 : 0;
-  uint32_t k_off[NCH], v_off[NCH];
+  uint32_t m_off[NCH / 2];
+  {
+    const int r = WROWS * warp + 8 * ((lane >> 3) & 1) + (lane & 7);
+    const int key = (r >> Cfg::SH) & Cfg::SWZ;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    k_off[c] = (WROWS * warp + g) * P_ + 16 * (c ^ kkey) + 4 * tg;
-    v_off[c] = (WROWS * warp + 2 * tg) * P_ + 16 * (c ^ vkey) + 2 * g;
+    for (int cp = 0; cp < NCH / 2; ++cp)
+      m_off[cp] = r * P_ + 16 * ((2 * cp + (lane >> 4)) ^ key);
   }
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
@@ -639,23 +639,28 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
     float sc[2][NG][4];  // first MMA of each group takes the bias as its C input
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int gi = c / CPG;
+    for (int cp = 0; cp < NCH / 2; ++cp) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t base = kp + k_off[c] + h * 16 * P_;
-        const uint32_t x0 = lds32(base), x1 = lds32(base + 8 * P_);
-        const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
-        const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
-        if (c % CPG == 0)
-          mma_bf16_16816_c(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
-                           bias[gi][1], bias[gi][0], bias[gi][1]);
-        else
-          mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
-        mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
-        if constexpr (SPLIT) {
-          mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
-          mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
+        uint32_t xr[4];  // x0, x1 of chunk 2cp, then of chunk 2cp+1
+        ldsm_x4(kp + m_off[cp] + h * 16 * P_, xr);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = 2 * cp + e;
+          const int gi = c / CPG;
+          const uint32_t x0 = xr[2 * e], x1 = xr[2 * e + 1];
+          const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
+          const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
+          if (c % CPG == 0)
+            mma_bf16_16816_c(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
+                             bias[gi][1], bias[gi][0], bias[gi][1]);
+          else
+            mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
+          mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
+          if constexpr (SPLIT) {
+            mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
+            mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
+          }
         }
       }
     }
@@ -762,21 +767,24 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
         }
       }
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        const uint32_t base = vp + v_off[c] + h * 16 * P_;
-        const uint32_t base1 = vp + v_off[c ^ VODD] + h * 16 * P_;  // odd rows
-        const uint32_t ha = lds16(base), hb = lds16(base1 + P_);
-        const uint32_t hc = lds16(base + 8 * P_), hd = lds16(base1 + 9 * P_);
-        const uint32_t wab = prmt(ha, hb, 0x5410);
-        const uint32_t wcd = prmt(hc, hd, 0x5410);
-        const int gi = c / CPG;
-        const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
-        const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
-        mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pb[gi][0], pb[gi][1]);
-        mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pb[gi][0], pb[gi][1]);
-        if constexpr (SPLIT) {
-          mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pbl[gi][0], pbl[gi][1]);
-          mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pbl[gi][0], pbl[gi][1]);
+      for (int cp = 0; cp < NCH / 2; ++cp) {
+        // transposed loads give [t.B0, t.B1, t+1.B0, t+1.B1] words directly:
+        // tokens 2tg, 2tg+1 (then +8, +9), bytes 2g, 2g+1 of the chunk
+        uint32_t wr[4];
+        ldsm_x4_trans(vp + m_off[cp] + h * 16 * P_, wr);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = 2 * cp + e;
+          const int gi = c / CPG;
+          const uint32_t wab = wr[2 * e], wcd = wr[2 * e + 1];
+          const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
+          const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
+          mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pb[gi][0], pb[gi][1]);
+          mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pb[gi][0], pb[gi][1]);
+          if constexpr (SPLIT) {
+            mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pbl[gi][0], pbl[gi][1]);
+            mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pbl[gi][0], pbl[gi][1]);
+          }
         }
       }
 #pragma unroll

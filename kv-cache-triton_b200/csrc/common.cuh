@@ -100,18 +100,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(1000000u)  // suspend-time hint (ns): sleep, do not spin
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each poll may suspend the thread
-// for a hardware-defined interval) and reports false.
+// Bounded wait: gives up after `limit` polls (each poll suspends the thread
+// until the phase completes or the 1 ms hint elapses) and reports false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  uint32_t limit = (1u << 22)) {
+                                                  uint32_t limit = (1u << 14)) {
   for (uint32_t it = 0; it < limit; ++it)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
@@ -187,6 +187,18 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(addr));
   return v;
+}
+
+// four 8x8 b16 matrices from shared memory (lanes 8j..8j+7 give matrix j's row addresses)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
