@@ -35,22 +35,39 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "kv-cache-triton_b200"))
 sys.path.insert(0, ROOT)
 
+# workloads: BASELINE config 2 (default) and config 3 (batch-1 long context)
+WORKLOADS = {
+    "config2": dict(B=16, HQ=32, HKV=8, S=4096),
+    "long16k": dict(B=1, HQ=32, HKV=8, S=16384),
+    "long64k": dict(B=1, HQ=32, HKV=8, S=65536),
+    "long128k": dict(B=1, HQ=32, HKV=8, S=131072),
+}
 B, HQ, HKV, S, D, G = 16, 32, 8, 4096, 128, 32
 LAYERS = 32
 METRIC = "INT4-KV decode attention HBM GB/s (Llama-3.1-8B shape, B16, S4096, G32)"
 
 
-def attn_bytes(b=B, hq=HQ, hkv=HKV, s=S, d=D, g=G, ss=2, qs=2):
+def attn_bytes(ss=2, qs=2):
     """Algorithmic bytes of one decode-attention launch: packed K/V + scales
     over the S-token cache, q read, output written."""
-    return 2 * b * hkv * s * (d // 2 + (d // g) * ss) + 2 * b * hq * d * qs
+    return 2 * B * HKV * S * (D // 2 + (D // G) * ss) + 2 * B * HQ * D * qs
 
 
-def append_bytes(b=B, hkv=HKV, d=D, g=G, ss=2, xs=2):
-    return 2 * b * hkv * (d * xs + d // 2 + (d // g) * ss)
+def append_bytes(ss=2, xs=2):
+    return 2 * B * HKV * (D * xs + D // 2 + (D // G) * ss)
 
 
-STEP_BYTES = attn_bytes() + append_bytes()
+def step_bytes():
+    return attn_bytes() + append_bytes()
+
+
+def set_workload(name):
+    global B, HQ, HKV, S, LAYERS, METRIC
+    w = WORKLOADS[name]
+    B, HQ, HKV, S = w["B"], w["HQ"], w["HKV"], w["S"]
+    # enough layer caches to keep ~2.4 GB resident (>> the 126 MB L2)
+    LAYERS = max(2, min(32, -(-2_400_000_000 // attn_bytes())))
+    METRIC = (f"INT4-KV decode attention HBM GB/s (Llama-3.1-8B shape, B{B}, S{S}, G{G})")
 
 
 def _dist():
@@ -173,34 +190,27 @@ def run_ours(args, ws, rank, local):
     for l in range(LAYERS):
         store.layer(l).seq_len = S
     p = ops.plan(q[0], *store.layer(0).views(), out, G, False)
-    # eager warm-up (caches occupancy queries / smem attributes), then one CUDA
-    # graph per (layer, op) so the timed loop is device-bound, not host-bound
+    # eager warm-up (caches occupancy queries / smem attributes), then CUDA
+    # graphs so the timed loops are device-bound, not host-bound: one graph
+    # per layer for a whole step (append + attention) and one per layer for
+    # the attention kernel alone (its own timing for the roofline)
     for l in range(LAYERS):
         append_op(l)
         attn_op(l)
     torch.cuda.synchronize()
-    g_app, g_att = [], []
+    g_step, g_att = [], []
     for l in range(LAYERS):
         ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         with torch.cuda.graph(ga):
             append_op(l)
+            attn_op(l)
         with torch.cuda.graph(gb):
             attn_op(l)
-        g_app.append(ga)
+        g_step.append(ga)
         g_att.append(gb)
-    n_ev = args.warmup + args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(n_ev)]
-
-    def step(i):
-        l = i % LAYERS
-        g_app[l].replay()
-        ev[i][0].record(st)
-        g_att[l].replay()
-        ev[i][1].record(st)
 
     for i in range(args.warmup):
-        step(i)
+        g_step[i % LAYERS].replay()
     torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
@@ -209,14 +219,24 @@ def run_ours(args, ws, rank, local):
     with ClockSampler(local) as clk:
         t0.record(st)
         for i in range(args.warmup, args.warmup + args.steps):
-            step(i)
+            g_step[i % LAYERS].replay()
         t1.record(st)
         torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
-    attn_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.warmup, n_ev)]
+    # the attention kernel alone, one event pair per launch, same rotation
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    for i in range(args.warmup):
+        g_att[i % LAYERS].replay()
+    for i in range(args.steps):
+        ev[i][0].record(st)
+        g_att[i % LAYERS].replay()
+        ev[i][1].record(st)
+    torch.cuda.synchronize()
+    attn_ms = [a.elapsed_time(b) for a, b in ev]
 
     # ---- e2e: public API, pinned host buffers in and out every step ----
     hq = torch.randn(args.steps, B, HQ, 1, D).to(torch.bfloat16).pin_memory()
@@ -268,7 +288,7 @@ def run_ours(args, ws, rank, local):
         return None
     peak, peak_kind = _peaks()
     per_step_ms = ms / args.steps
-    value = ws * STEP_BYTES * args.steps / (ms * 1e-3) / 1e9
+    value = ws * step_bytes() * args.steps / (ms * 1e-3) / 1e9
     achieved = attn_bytes() / (attn_avg_ms * 1e-3) / 1e9
     h2d = (B * HQ * D + 2 * B * HKV * D) * 2
     d2h = B * HQ * D * 2
@@ -286,21 +306,21 @@ def run_ours(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
         "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
-        "config": {"workload": "llama3.1-8b single-layer decode: append 1 token + fused INT4 "
-                               "decode attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+        "config": {"workload": f"{args.workload}: llama3.1-8b single-layer decode: append 1 "
+                               "token + fused INT4 decode attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
                    "seq_len": S, "d_head": D, "group_size": G,
                    "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
                    "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
                          f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
-                   "bytes_per_step": STEP_BYTES},
+                   "bytes_per_step": step_bytes()},
         "gpu_launches": args.steps * (1 + int(p.kernels)),
-        "e2e": {"value": round(ws * STEP_BYTES * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
+        "e2e": {"value": round(ws * step_bytes() * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": _traffic()},
+                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": _traffic() if args.workload == "config2" else None},
         "clocks": clk.summary(),
         "plan": {"path": int(p.path), "ctas": int(p.ctas), "tiles_per_cta": int(p.tiles_per_cta),
                  "kernels_per_attention": int(p.kernels)},
@@ -311,6 +331,7 @@ def run_ours(args, ws, rank, local):
 
 
 def cpu_baseline(budget_s: float = 15.0, batch_sample: int = 2):
+    batch_sample = min(batch_sample, B)
     """The reference's CPU formulation on a batch slice of config 2, all host threads."""
     from oracle import torch_ref
     threads = os.cpu_count() or 1
@@ -336,7 +357,7 @@ def cpu_baseline(budget_s: float = 15.0, batch_sample: int = 2):
     per_sample = el / n
     frac = batch_sample / B
     step_s = per_sample / frac
-    return {"value": round(STEP_BYTES / step_s / 1e9, 3), "unit": "GB/s",
+    return {"value": round(step_bytes() / step_s / 1e9, 3), "unit": "GB/s",
             "us_per_step": round(step_s * 1e6, 1), "cores": threads, "kind": "port",
             "sample": f"{n} decode steps of batch {batch_sample}/{B} (S={S}) with the reference's "
                       f"torch CPU path (quantize+cat+dequant+SDPA), scaled x{B // batch_sample}"}
@@ -366,7 +387,7 @@ def run_reference(args, ws, rank):
         torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
     el = time.perf_counter() - t0
     step_s = el / args.steps * (B / bs)  # per full config-2 step
-    value = STEP_BYTES / step_s / 1e9
+    value = step_bytes() / step_s / 1e9
     sample = (f"each step = batch {bs}/{B} of config 2 (S={S}) through the reference's torch "
               f"CPU path (quantize+cat+dequant+repeat_interleave+SDPA); rate scaled to the "
               f"full batch")
@@ -394,7 +415,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
+                    help="config2 = BASELINE config 2 (the headline); long* = config 3")
     args = ap.parse_args()
+    set_workload(args.workload)
     args.warmup = max(args.warmup, 3)
     ws, rank, local = _dist()
     if args.impl == "reference":

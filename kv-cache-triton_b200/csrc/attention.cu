@@ -461,19 +461,19 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       for (int e = 0; e < 4; ++e) sp_acc[gi][e] = 0.0f;
   };
 
-  // Finish the current unit segment: merge the 4 warps through smem, then
-  // either write the output (unit wholly inside this CTA) or write a partial
-  // slot; the last CTA to finish a split unit (per-unit counter) merges all
-  // of the unit's slots and writes the output, then re-arms the counter.
+  // Finish the CTA's unit segment: merge the 4 warps through smem, then
+  // either write the output (unit wholly inside this CTA) or a partial slot;
+  // the last CTA to finish a split unit (per-unit counter) merges all of the
+  // unit's slots in one pass (online log-sum-exp) and re-arms the counter.
   auto flush = [&]() {
     const int hcid = u_hc, b = u_b, kvh = u_kvh;
-    __syncthreads();  // merge_o aliases the stages other warps may still be reading
 #pragma unroll
     for (int j = 0; j < 2; ++j) {  // l over the 8 token-row lanes
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
     }
+    __syncthreads();  // merge_o aliases the stages other warps may still be reading
     if (g == 0) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -481,7 +481,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
         merge_l[warp * NCOL + 2 * tg + j] = l_run[j];
       }
     }
-    // O^T fragment -> smem [warp][col][dim]; remove the +128 code bias
+    // O^T fragment -> smem [warp][col][dim] (dims d0, d0+1 as one float2);
+    // remove the +128 code bias
     float *mo = merge_o + warp * NCOL * D;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -492,8 +493,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {  // column 2tg + cc
           const float corr = 136.0f * sp_acc[gi][cc];
-          mo[(2 * tg + cc) * D + d0] = o_acc[c][j][cc] - corr;
-          mo[(2 * tg + cc) * D + d0 + 1] = o_acc[c][j][2 + cc] - corr;
+          *reinterpret_cast<float2 *>(&mo[(2 * tg + cc) * D + d0]) =
+              make_float2(o_acc[c][j][cc] - corr, o_acc[c][j][2 + cc] - corr);
         }
       }
     }
@@ -516,20 +517,28 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       merge_lse[tid] = Lsum > 0.0f ? M + log2f(Lsum) : kNegInf;
     }
     __syncthreads();
-    for (int idx = tid; idx < NCOL * D; idx += blockDim.x) {
-      const int col = idx / D, dd = idx % D;
+    constexpr int D4 = D / 4;
+    for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
+      const int col = idx / D4, d4 = idx - col * D4;
       const int n = hcid * NCOL + col;
       if (n >= P.ncols) continue;
-      float val = 0.0f;
+      float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int w = 0; w < NWARP; ++w) val += merge_o[(w * NCOL + col) * D + dd] * merge_f[w * NCOL + col];
-      const int qi = n / C.R, h = kvh * C.R + n % C.R;
+      for (int w = 0; w < NWARP; ++w) {
+        const float4 x = *reinterpret_cast<const float4 *>(&merge_o[(w * NCOL + col) * D + 4 * d4]);
+        const float f = merge_f[w * NCOL + col];
+        val.x += f * x.x; val.y += f * x.y; val.z += f * x.z; val.w += f * x.w;
+      }
       if (whole) {
-        emit_value(C, b, h, qi, dd, val);
-        if (dd == 0) emit_lse(C, b, h, qi, merge_lse[col]);
+        const int qi = n / C.R, h = kvh * C.R + n % C.R;
+        emit_value(C, b, h, qi, 4 * d4, val.x);
+        emit_value(C, b, h, qi, 4 * d4 + 1, val.y);
+        emit_value(C, b, h, qi, 4 * d4 + 2, val.z);
+        emit_value(C, b, h, qi, 4 * d4 + 3, val.w);
+        if (d4 == 0) emit_lse(C, b, h, qi, merge_lse[col]);
       } else {
-        P.ws_o[(static_cast<int64_t>(slot) * NCOL + col) * D + dd] = val;
-        if (dd == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = merge_lse[col];
+        reinterpret_cast<float4 *>(P.ws_o + (static_cast<int64_t>(slot) * NCOL + col) * D)[d4] = val;
+        if (d4 == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = merge_lse[col];
       }
     }
     if (!whole) {
@@ -544,58 +553,45 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       }
       __syncthreads();
       if (sh_last) {
-        const int nparts = kparts;
         const int64_t slot0 = static_cast<int64_t>(u) * kparts;
-        float *wts = reinterpret_cast<float *>(smem);  // stage buffers are idle now
-        for (int k = tid; k < nparts * NCOL; k += blockDim.x)
-          wts[k] = __ldcg(&P.ws_lse[slot0 * NCOL + k]);
-        __syncthreads();
-        if (tid < NCOL) {
-          float M = kNegInf;
-          for (int p = 0; p < nparts; ++p) M = fmaxf(M, wts[p * NCOL + tid]);
-          float W = 0.0f;
-          for (int p = 0; p < nparts; ++p) {
-            const float w = (M == kNegInf) ? 0.0f : exp2f(wts[p * NCOL + tid] - M);
-            wts[p * NCOL + tid] = w;
-            W += w;
-          }
-          const float inv = W > 0.0f ? 1.0f / W : 0.0f;
-          for (int p = 0; p < nparts; ++p) wts[p * NCOL + tid] *= inv;
-          merge_lse[tid] = W > 0.0f ? M + log2f(W) : kNegInf;
-        }
-        __syncthreads();
-        constexpr int D4 = D / 4;
         for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
-          const int col = idx / D4, d4 = idx % D4;
+          const int col = idx / D4, d4 = idx - col * D4;
           const int n = hcid * NCOL + col;
           if (n >= P.ncols) continue;
           const float4 *src =
               reinterpret_cast<const float4 *>(P.ws_o + (slot0 * NCOL + col) * D) + d4;
-          const int pstride = NCOL * D4;
+          const float *lsrc = P.ws_lse + slot0 * NCOL + col;
+          // online log-sum-exp over the parts, 8 loads in flight per round
+          float M = kNegInf, W = 0.0f;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          int p = 0;
-          for (; p + 4 <= nparts; p += 4) {  // four loads in flight per step
-            float4 v[4];
+          for (int p0 = 0; p0 < kparts; p0 += 8) {
+            float4 v[8];
+            float lp[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] = __ldcg(src + (p + e) * pstride);
+            for (int e = 0; e < 8; ++e) {
+              const int p = min(p0 + e, kparts - 1);
+              v[e] = __ldcg(src + static_cast<int64_t>(p) * NCOL * D4);
+              lp[e] = (p0 + e < kparts) ? __ldcg(lsrc + static_cast<int64_t>(p) * NCOL) : kNegInf;
+            }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float w = wts[(p + e) * NCOL + col];
-              acc.x += w * v[e].x; acc.y += w * v[e].y; acc.z += w * v[e].z; acc.w += w * v[e].w;
+            for (int e = 0; e < 8; ++e) {
+              const float mn = fmaxf(M, lp[e]);
+              if (mn == kNegInf) continue;
+              const float a = exp2f(M - mn), w = exp2f(lp[e] - mn);
+              W = W * a + w;
+              acc.x = acc.x * a + w * v[e].x; acc.y = acc.y * a + w * v[e].y;
+              acc.z = acc.z * a + w * v[e].z; acc.w = acc.w * a + w * v[e].w;
+              M = mn;
             }
           }
-          for (; p < nparts; ++p) {
-            const float4 v = __ldcg(src + p * pstride);
-            const float w = wts[p * NCOL + col];
-            acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-          }
+          const float inv = W > 0.0f ? 1.0f / W : 0.0f;
           const int qi = n / C.R, h = kvh * C.R + n % C.R;
           const int dd = 4 * d4;
-          emit_value(C, b, h, qi, dd, acc.x);
-          emit_value(C, b, h, qi, dd + 1, acc.y);
-          emit_value(C, b, h, qi, dd + 2, acc.z);
-          emit_value(C, b, h, qi, dd + 3, acc.w);
-          if (dd == 0) emit_lse(C, b, h, qi, merge_lse[col]);
+          emit_value(C, b, h, qi, dd, acc.x * inv);
+          emit_value(C, b, h, qi, dd + 1, acc.y * inv);
+          emit_value(C, b, h, qi, dd + 2, acc.z * inv);
+          emit_value(C, b, h, qi, dd + 3, acc.w * inv);
+          if (dd == 0) emit_lse(C, b, h, qi, W > 0.0f ? M + log2f(W) : kNegInf);
         }
       }
     }

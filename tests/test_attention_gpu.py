@@ -204,3 +204,32 @@ def test_no_device_error_flag_after_runs():
     from kvint4 import ops
     _run(2, 8, 2, 1, 500, 128, 32, torch.bfloat16)
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("sk", [16384, 131072])
+def test_config3_long_context_batch1(sk):
+    """BASELINE config 3 shape (B=1, 32/8 heads, d=128, G=32) at full length:
+    KV head 0 (q heads 0-3) against the oracle, plus agreement of the fused
+    kernel with a 4-way sequence-shard decomposition for all heads."""
+    from kvint4 import ops
+    from kvint4.cache import Int4KVStore
+    from kvint4.shard import shard_range
+    k, v = kv_inputs(1, 8, sk, 128, device="cuda", seed=sk % 97)
+    st = Int4KVStore(32)
+    st.append(k, v, 0)
+    kp, ks, vp, vs = st.layer(0).views()
+    q = torch.randn(1, 32, 1, 128, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ops.attention_into(q, kp, ks, vp, vs, out, 32)
+    ref = oracle_attention(q[:, :4], kp[:, :1], ks[:, :1], vp[:, :1], vs[:, :1], n_q_heads=4,
+                           n_kv_heads=1, group_size=32)
+    np.testing.assert_allclose(f32(out[:, :4]), ref, atol=2e-2, rtol=0)
+    po = torch.empty(4, 1, 32, 1, 128, device="cuda")
+    pl = torch.empty(4, 1, 32, 1, device="cuda")
+    for r in range(4):
+        a, e = shard_range(sk, 4, r)
+        ops.attention_partial_into(q, kp[:, :, a:e], ks[:, :, a:e], vp[:, :, a:e], vs[:, :, a:e],
+                                   po[r], pl[r], a, sk, 32)
+    comb = torch.empty_like(q)
+    ops.lse_combine_into(po.reshape(4, -1, 128), pl.reshape(4, -1), comb)
+    assert (comb.float() - out.float()).abs().max().item() <= 2e-2
