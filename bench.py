@@ -5,8 +5,9 @@
 Workload (per rank): Llama-3.1-8B single-layer decode, B=16, 32 q heads,
 8 KV heads, d=128, context S=4096, INT4 group size 32, bf16 q/K/V, K
 channels scaled by log-uniform [0.5, 8] factors, seeded synthetic data.  A
-step = quantize-append of the new K/V token (one launch) + fused decode
-attention over the S-token INT4 cache, for one layer.  Steps rotate over 32
+step = quantize-append of the new K/V token + fused decode attention over
+the S-token INT4 cache, for one layer, in ONE launch (kv4_append_attention:
+the attention kernel quantizes the new row itself).  Steps rotate over 32
 layer caches (2.4 GB resident per GPU), so every step reads its cache from
 HBM, not L2 (126 MB).
 
@@ -167,7 +168,6 @@ def build_caches(dev, seed=0):
 
 
 def run_ours(args, ws, rank, local):
-    from kernels.llama3.attention_quant import attention_forward_quant_gqa
     from kvint4 import ops
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -187,27 +187,32 @@ def run_ours(args, ws, rank, local):
         kp, ks, vp, vs = store.layer(l).views()
         ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
 
+    def step_op(l):  # the product's decode step: append fused into the attention launch
+        kp, ks, vp, vs = store.layer(l).views()
+        ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False)
+
     for l in range(LAYERS):
         store.layer(l).seq_len = S
     p = ops.plan(q[0], *store.layer(0).views(), out, G, False)
     # eager warm-up (caches occupancy queries / smem attributes), then CUDA
     # graphs so the timed loops are device-bound, not host-bound: one graph
-    # per layer for a whole step (append + attention) and one per layer for
-    # the attention kernel alone (its own timing for the roofline)
+    # per layer for the step, and, for comparison, one per layer for the
+    # unfused pair (append kernel + attention kernel)
     for l in range(LAYERS):
+        step_op(l)
         append_op(l)
         attn_op(l)
     torch.cuda.synchronize()
-    g_step, g_att = [], []
+    g_step, g_pair = [], []
     for l in range(LAYERS):
         ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         with torch.cuda.graph(ga):
+            step_op(l)
+        with torch.cuda.graph(gb):
             append_op(l)
             attn_op(l)
-        with torch.cuda.graph(gb):
-            attn_op(l)
         g_step.append(ga)
-        g_att.append(gb)
+        g_pair.append(gb)
 
     for i in range(args.warmup):
         g_step[i % LAYERS].replay()
@@ -226,17 +231,21 @@ def run_ours(args, ws, rank, local):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
-    # the attention kernel alone, one event pair per launch, same rotation
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    for i in range(args.warmup):
-        g_att[i % LAYERS].replay()
-    for i in range(args.steps):
-        ev[i][0].record(st)
-        g_att[i % LAYERS].replay()
-        ev[i][1].record(st)
-    torch.cuda.synchronize()
-    attn_ms = [a.elapsed_time(b) for a, b in ev]
+
+    def per_launch(graphs):  # one event pair per replay, same layer rotation
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for i in range(args.warmup):
+            graphs[i % LAYERS].replay()
+        for i in range(args.steps):
+            ev[i][0].record(st)
+            graphs[i % LAYERS].replay()
+            ev[i][1].record(st)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in ev]
+
+    attn_ms = per_launch(g_step)   # the fused kernel alone (roofline)
+    pair_ms = per_launch(g_pair)   # unfused append + attention, for comparison
 
     # ---- e2e: public API, pinned host buffers in and out every step ----
     hq = torch.randn(args.steps, B, HQ, 1, D).to(torch.bfloat16).pin_memory()
@@ -253,16 +262,15 @@ def run_ours(args, ws, rank, local):
     dk = torch.empty(B, HKV, 1, D, dtype=torch.bfloat16, device=dev)
     dv = torch.empty_like(dk)
 
+    do = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+
     def e2e_step(i):
         c = caches[i % LAYERS]
         c._store.layer(0).seq_len = S - 1
         dq.copy_(hq[i % args.steps], non_blocking=True)
         dk.copy_(hk[i % args.steps], non_blocking=True)
         dv.copy_(hv[i % args.steps], non_blocking=True)
-        c.append(dk, dv, 0)
-        kp, ks, vp, vs = c.get_quantized(0)
-        o = attention_forward_quant_gqa(dq, kp, ks, vp, vs, n_q_heads=HQ, n_kv_heads=HKV,
-                                        group_size=G)
+        o = c.append_attend(dq, dk, dv, 0, do, n_q_heads=HQ, n_kv_heads=HKV)
         hout[i % args.steps].copy_(o, non_blocking=True)
 
     for i in range(args.warmup):
@@ -279,17 +287,18 @@ def run_ours(args, ws, rank, local):
     e2e_ms = e0.elapsed_time(e1)
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms, statistics.mean(attn_ms)], device=dev)
+    t = torch.tensor([ms, e2e_ms, statistics.mean(attn_ms), statistics.mean(pair_ms)],
+                     device=dev)
     if ws > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.barrier()
-    ms, e2e_ms, attn_avg_ms = (float(x) for x in t.tolist())
+    ms, e2e_ms, attn_avg_ms, pair_avg_ms = (float(x) for x in t.tolist())
     if rank != 0:
         return None
     peak, peak_kind = _peaks()
     per_step_ms = ms / args.steps
     value = ws * step_bytes() * args.steps / (ms * 1e-3) / 1e9
-    achieved = attn_bytes() / (attn_avg_ms * 1e-3) / 1e9
+    achieved = step_bytes() / (attn_avg_ms * 1e-3) / 1e9
     h2d = (B * HQ * D + 2 * B * HKV * D) * 2
     d2h = B * HQ * D * 2
     line = {
@@ -307,20 +316,22 @@ def run_ours(args, ws, rank, local):
         "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
         "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
         "config": {"workload": f"{args.workload}: llama3.1-8b single-layer decode: append 1 "
-                               "token + fused INT4 decode attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                               "token + INT4 decode attention, one fused launch", "batch": B, "q_heads": HQ, "kv_heads": HKV,
                    "seq_len": S, "d_head": D, "group_size": G,
                    "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
                    "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
                          f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
                    "bytes_per_step": step_bytes()},
-        "gpu_launches": args.steps * (1 + int(p.kernels)),
+        "gpu_launches": args.steps * int(p.kernels),
         "e2e": {"value": round(ws * step_bytes() * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "attn_us": round(attn_avg_ms * 1e3, 2), "traffic": _traffic() if args.workload == "config2" else None},
+                     "kernel_us": round(attn_avg_ms * 1e3, 2),
+                     "unfused_append_plus_attention_us": round(pair_avg_ms * 1e3, 2),
+                     "traffic": _traffic() if args.workload == "config2" else None},
         "clocks": clk.summary(),
         "plan": {"path": int(p.path), "ctas": int(p.ctas), "tiles_per_cta": int(p.tiles_per_cta),
                  "kernels_per_attention": int(p.kernels)},

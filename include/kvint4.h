@@ -147,6 +147,27 @@ int kv4_attention_plan(const kv4_tensor *q, const kv4_tensor *k_packed,
                        int is_causal, const kv4_attn_opts *opts, kv4_attn_plan *plan);
 
 /*
+ * Decode step with the quantize-on-append fused in: k_new/v_new
+ * [B, Hkv, n, d] (float, one dtype) are quantized into the LAST n rows of
+ * k_packed/k_scales/v_packed/v_scales (views of sk rows that already include
+ * the new positions, e.g. capacity buffers sliced to [:, :, :sk]), then q
+ * attends over all sk rows; results equal kv4_append_kv(..., pos = sk - n)
+ * followed by kv4_attention.  With n == 1, unit dim stride and the fast
+ * path (kv4_attention_plan().path == 1) both run in ONE launch (every CTA
+ * that stages the new row quantizes it itself; one CTA per (b, kv head)
+ * writes it to the cache); otherwise the append kernel runs first on the
+ * same stream.  Replaces the reference's per-layer decode sequence
+ * QuantizedKVCache.update (models/llama3/kv_cache.py:76-102) followed by
+ * attention_forward_quant_gqa (models/llama3/llama3_quant.py:59-99).
+ */
+int kv4_append_attention(const kv4_tensor *q, const kv4_tensor *k_new, const kv4_tensor *v_new,
+                         const kv4_tensor *k_packed, const kv4_tensor *k_scales,
+                         const kv4_tensor *v_packed, const kv4_tensor *v_scales,
+                         const kv4_tensor *out, int group_size, int tie_mode, int is_causal,
+                         float sm_scale, void *workspace, size_t workspace_bytes,
+                         const kv4_attn_opts *opts, void *stream);
+
+/*
  * Sequence-shard partial of kv4_attention (new; the reference has no
  * multi-GPU layer, it relies on accelerate device_map placement,
  * benchmarks/llama3/run_llama3_benchmark.py:115-121).  The cache slice holds

@@ -195,7 +195,74 @@ struct FastParams {
   int *counters;  // [units] finished-segment counts (zero between calls)
   const char *ks, *vs;         // scale tensors
   int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
+  // Fused quantize-on-append (app_row >= 0): the new token's K/V rows
+  // (kn/vn [B, Hkv, 1, d], unit dim stride) are quantized into cache row
+  // app_row.  Every CTA that streams that row quantizes it itself and patches
+  // its staged copy; the hc == 0 CTA of the (b, kvh) also writes it to HBM.
+  int app_row;
+  int app_tie;
+  int kn_dtype;
+  const void *kn, *vn;
+  int64_t kn_sb, kn_sh, vn_sb, vn_sh;  // elements
+  uint8_t *kpw, *vpw;                  // packed caches (bytes)
+  int64_t kp_sb, kp_sh, kp_st, vp_sb, vp_sh, vp_st;
 };
+
+// Quantize one d-wide row with a warp: lane l owns dims [DPL*l, DPL*l + DPL)
+// and returns their packed nibbles (low nibble = even dim) and its group's
+// fp32 scale.  Same arithmetic as quantize_kernel (max |x| / 7, IEEE division).
+template <int D, int G>
+__device__ __forceinline__ void quant_row_warp(const void *x, int dt, int64_t off, int tie,
+                                               int lane, uint32_t &w, float &scale) {
+  constexpr int DPL = D / 32, LPG = G / DPL;
+  float v[DPL];
+  float mx = 0.0f;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) {
+    v[e] = load_as_f32(x, dt, off + DPL * lane + e);
+    mx = fmaxf(mx, fabsf(v[e]));
+  }
+#pragma unroll
+  for (int o = 1; o < LPG; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  scale = mx > 0.0f ? __fdiv_rn(mx, 7.0f) : 1.0f;
+  w = 0;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e)
+    w |= (tie == KV4_TIE_HALF_EVEN ? code_of<KV4_TIE_HALF_EVEN>(v[e], scale)
+                                   : code_of<KV4_TIE_HALF_AWAY>(v[e], scale))
+         << (4 * e);
+}
+
+// store the DPL/2 low bytes of w (1, 2 or 4; the address is aligned to that)
+template <int NB>
+__device__ __forceinline__ void st_bytes_global(uint8_t *p, uint32_t w) {
+  if constexpr (NB == 1) *p = static_cast<uint8_t>(w);
+  else if constexpr (NB == 2) *reinterpret_cast<uint16_t *>(p) = static_cast<uint16_t>(w);
+  else *reinterpret_cast<uint32_t *>(p) = w;
+}
+template <int NB>
+__device__ __forceinline__ void st_bytes_shared(uint32_t a, uint32_t w) {
+  if constexpr (NB == 1) asm volatile("st.shared.u8 [%0], %1;" ::"r"(a), "r"(w) : "memory");
+  else if constexpr (NB == 2) asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "r"(w) : "memory");
+  else asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(w) : "memory");
+}
+template <int NB>
+__device__ __forceinline__ uint32_t ld_bytes_shared(uint32_t a) {
+  uint32_t w;
+  if constexpr (NB == 1) asm volatile("ld.shared.u8 %0, [%1];" : "=r"(w) : "r"(a) : "memory");
+  else if constexpr (NB == 2) asm volatile("ld.shared.u16 %0, [%1];" : "=r"(w) : "r"(a) : "memory");
+  else asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(a) : "memory");
+  return w;
+}
+template <typename ST>
+__device__ __forceinline__ void st_scale_shared(uint32_t a, ST v) {
+  if constexpr (sizeof(ST) == 2) {
+    const uint32_t b = *reinterpret_cast<const uint16_t *>(&v);
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "r"(b) : "memory");
+  } else {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(static_cast<float>(v)) : "memory");
+  }
+}
 
 // Shared-memory layout of one stage (per tensor): packed codes token-major
 // [token][P bytes] as TMA writes them with the P-byte swizzle (16-byte chunk c
@@ -217,8 +284,9 @@ struct FastCfg {
   static constexpr int STAGES = 2;  // 2 x 18 KB (d=128) keeps 4 CTAs/SM resident
   static constexpr int MERGE = NWARP * NCOL * D * 4;
   static_assert(MERGE <= STAGES * STAGE, "merge buffer aliases the stages");
+  static constexpr int APP = 2 * P + 2 * SROW;  // staged new row (fused append)
   static constexpr int SMEM = STAGES * STAGE + 3 * NWARP * NCOL * 4 + 2 * NCOL * 4 +
-                              16 * STAGES + 1024;
+                              16 * STAGES + APP + 1024;
   static constexpr uint32_t TX = 2 * KP + 2 * KS;
 };
 
@@ -303,6 +371,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   float *merge_f = merge_l + NWARP * NCOL;
   float *merge_lse = merge_f + NWARP * NCOL;
   uint64_t *bars = reinterpret_cast<uint64_t *>(merge_lse + 2 * NCOL);  // full[S], empty[S]
+  // fused append: quantized new row [K codes P][V codes P][K scales][V scales]
+  uint8_t *app_buf = reinterpret_cast<uint8_t *>(bars + 2 * Cfg::STAGES);
   __shared__ int sh_abort;
   __shared__ int sh_last;
 
@@ -358,6 +428,51 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   if (tid == 0) {
     const int pre = min(ntiles, Cfg::STAGES);
     for (int i = 0; i < pre; ++i) issue(i);
+  }
+
+  // ---- fused append: the owner warp of the new row quantizes it once ----
+  // into app_buf (and, for hc == 0, into the cache in HBM); the same warp
+  // copies it over the staged row once that tile has landed.
+  constexpr int DPL = D / 32, NBL = DPL / 2;  // dims / packed bytes per lane
+  int app_key = -1;                           // (local tile) * NWARP + owner warp
+  {
+    const int app_tile = P.app_row >= 0 ? P.app_row / TOK : -1;
+    if (app_tile >= t_begin && app_tile < t_end) {
+      const int app_warp = (P.app_row - app_tile * TOK) / WROWS;
+      app_key = (app_tile - t_begin) * NWARP + app_warp;
+      if (warp == app_warp) {
+        uint32_t kw, vw;
+        float ksf, vsf;
+        quant_row_warp<D, G>(P.kn, P.kn_dtype, u_b * P.kn_sb + u_kvh * P.kn_sh, P.app_tie, lane,
+                             kw, ksf);
+        quant_row_warp<D, G>(P.vn, P.kn_dtype, u_b * P.vn_sb + u_kvh * P.vn_sh, P.app_tie, lane,
+                             vw, vsf);
+        const ST kst = from_f32<ST>(ksf), vst = from_f32<ST>(vsf);
+        const uint32_t ab = smem_u32(app_buf);
+        st_bytes_shared<NBL>(ab + NBL * lane, kw);
+        st_bytes_shared<NBL>(ab + Cfg::P + NBL * lane, vw);
+        const bool lead = (DPL * lane) % G == 0;
+        const int so = (DPL * lane / G) * static_cast<int>(sizeof(ST));
+        if (lead) {
+          st_scale_shared<ST>(ab + 2 * Cfg::P + so, kst);
+          st_scale_shared<ST>(ab + 2 * Cfg::P + Cfg::SROW + so, vst);
+        }
+        if (u_hc == 0) {  // one writer per (b, kvh) row
+          const int64_t r = P.app_row;
+          st_bytes_global<NBL>(P.kpw + u_b * P.kp_sb + u_kvh * P.kp_sh + r * P.kp_st + NBL * lane,
+                               kw);
+          st_bytes_global<NBL>(P.vpw + u_b * P.vp_sb + u_kvh * P.vp_sh + r * P.vp_st + NBL * lane,
+                               vw);
+          if (lead) {
+            *reinterpret_cast<ST *>(const_cast<char *>(P.ks) + u_b * P.ks_sb + u_kvh * P.ks_sh +
+                                    r * Cfg::SROW + so) = kst;
+            *reinterpret_cast<ST *>(const_cast<char *>(P.vs) + u_b * P.vs_sb + u_kvh * P.vs_sh +
+                                    r * Cfg::SROW + so) = vst;
+          }
+        }
+        __syncwarp();
+      }
+    }
   }
 
   // ---- per-unit state --------------------------------------------------
@@ -631,7 +746,24 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     const uint32_t ksb = kp + 2 * Cfg::KP;
     const uint32_t vsb = ksb + Cfg::KS;
     const int tok0 = ti * TOK + WROWS * warp;  // first token row of this warp
-
+    if (i * NWARP + warp == app_key) {
+      // the staged copy of the new row came from HBM before (or while) it was
+      // written: overwrite it with this warp's own quantization
+      const int r = P.app_row - ti * TOK;
+      const int o = NBL * lane;
+      const uint32_t off = r * P_ + 16 * ((o >> 4) ^ ((r >> Cfg::SH) & Cfg::SWZ)) + (o & 15);
+      const uint32_t ab = smem_u32(app_buf);
+      st_bytes_shared<NBL>(kp + off, ld_bytes_shared<NBL>(ab + o));
+      st_bytes_shared<NBL>(vp + off, ld_bytes_shared<NBL>(ab + Cfg::P + o));
+      if (lane < Cfg::SROW / 2) {  // scale rows, 2 bytes per lane
+        const uint32_t so = r * Cfg::SROW + 2 * lane;
+        st_bytes_shared<2>(ksb + so, ld_bytes_shared<2>(ab + 2 * Cfg::P + 2 * lane));
+        st_bytes_shared<2>(vsb + so, ld_bytes_shared<2>(ab + 2 * Cfg::P + Cfg::SROW + 2 * lane));
+      }
+      // order these generic writes before the TMA refill of the stage
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+    }
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
     float sc[2][NG][4];  // first MMA of each group takes the bias as its C input
 #pragma unroll
@@ -1084,14 +1216,34 @@ static int launch_fast_st(const FastParams &FP, const Plan &pl, const kv4_tensor
   return KV4_ERR_UNSUPPORTED;
 }
 
+// New tokens appended into the last rows of the cache views before attention.
+struct AppendJob {
+  const kv4_tensor *k, *v;  // [B, Hkv, n, d]
+  int tie;
+};
+
+static int check_append(const AppendJob &A, const Shape &S) {
+  if (!A.k || !A.v) return KV4_ERR_INVALID;
+  if (A.tie != KV4_TIE_HALF_AWAY && A.tie != KV4_TIE_HALF_EVEN) return KV4_ERR_INVALID;
+  if (!is_float(A.k->dtype) || A.v->dtype != A.k->dtype) return KV4_ERR_DTYPE;
+  for (int i = 0; i < 4; ++i)
+    if (A.k->shape[i] != A.v->shape[i]) return KV4_ERR_SHAPE;
+  if (A.k->shape[0] != S.B || A.k->shape[1] != S.Hkv || A.k->shape[3] != S.d)
+    return KV4_ERR_SHAPE;
+  if (A.k->shape[2] < 1 || A.k->shape[2] > S.sk) return KV4_ERR_SHAPE;
+  return KV4_OK;
+}
+
 static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
                          const kv4_tensor *vp, const kv4_tensor *vs, const kv4_tensor *out,
                          const kv4_tensor *lse, int mode, int64_t k_offset, int64_t sk_total,
                          int G, int is_causal, float sm_scale, void *ws, size_t ws_bytes,
-                         const kv4_attn_opts *opts, cudaStream_t st) {
+                         const kv4_attn_opts *opts, cudaStream_t st,
+                         const AppendJob *app = nullptr) {
   Shape S;
   int rc = validate(q, kp, ks, vp, vs, G, S);
   if (rc) return rc;
+  if (app && (rc = check_append(*app, S))) return rc;
   if (!out) return KV4_ERR_INVALID;
   for (int i = 0; i < 4; ++i)
     if (out->shape[i] != q->shape[i]) return KV4_ERR_SHAPE;
@@ -1134,9 +1286,38 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
 
   Plan pl;
   make_plan(q, kp, ks, vp, vs, S, opts, pl);
+  // one new token on the fast path is quantized inside the attention launch;
+  // anything else is appended by the quantize kernel first (same stream)
+  const bool fuse_app = app && pl.path == 1 && app->k->shape[2] == 1 &&
+                        app->k->stride[3] == 1 && app->v->stride[3] == 1;
+  if (pl.path == 1 && pl.ws_bytes > 0 && (ws == nullptr || ws_bytes < pl.ws_bytes))
+    return KV4_ERR_WORKSPACE;
+  if (app && !fuse_app) {
+    rc = kv4_append_kv(app->k, app->v, kp, ks, vp, vs, S.sk - app->k->shape[2], G, app->tie, st);
+    if (rc) return rc;
+  }
   if (pl.path == 1) {
-    if (pl.ws_bytes > 0 && (ws == nullptr || ws_bytes < pl.ws_bytes)) return KV4_ERR_WORKSPACE;
     FastParams FP{};
+    FP.app_row = -1;
+    if (fuse_app) {
+      FP.app_row = static_cast<int>(S.sk - 1);
+      FP.app_tie = app->tie;
+      FP.kn_dtype = app->k->dtype;
+      FP.kn = app->k->data;
+      FP.vn = app->v->data;
+      FP.kn_sb = app->k->stride[0];
+      FP.kn_sh = app->k->stride[1];
+      FP.vn_sb = app->v->stride[0];
+      FP.vn_sh = app->v->stride[1];
+      FP.kpw = static_cast<uint8_t *>(kp->data);
+      FP.vpw = static_cast<uint8_t *>(vp->data);
+      FP.kp_sb = kp->stride[0];
+      FP.kp_sh = kp->stride[1];
+      FP.kp_st = kp->stride[2];
+      FP.vp_sb = vp->stride[0];
+      FP.vp_sh = vp->stride[1];
+      FP.vp_st = vp->stride[2];
+    }
     FP.c = Cm;
     FP.ncols = pl.ncols;
     FP.hc = pl.hc;
@@ -1200,6 +1381,19 @@ extern "C" int kv4_attention(const kv4_tensor *q, const kv4_tensor *k_packed,
   return run_attention(q, k_packed, k_scales, v_packed, v_scales, out, nullptr, OUT_FINAL, 0, 0,
                        group_size, is_causal, sm_scale, workspace, workspace_bytes, opts,
                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kv4_append_attention(const kv4_tensor *q, const kv4_tensor *k_new,
+                                    const kv4_tensor *v_new, const kv4_tensor *k_packed,
+                                    const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                                    const kv4_tensor *v_scales, const kv4_tensor *out,
+                                    int group_size, int tie_mode, int is_causal, float sm_scale,
+                                    void *workspace, size_t workspace_bytes,
+                                    const kv4_attn_opts *opts, void *stream) {
+  const AppendJob app{k_new, v_new, tie_mode};
+  return run_attention(q, k_packed, k_scales, v_packed, v_scales, out, nullptr, OUT_FINAL, 0, 0,
+                       group_size, is_causal, sm_scale, workspace, workspace_bytes, opts,
+                       static_cast<cudaStream_t>(stream), &app);
 }
 
 extern "C" int kv4_attention_partial(const kv4_tensor *q, const kv4_tensor *k_packed,

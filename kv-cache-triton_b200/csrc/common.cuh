@@ -241,4 +241,19 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return r;
 }
 
+// INT4 code of x for a group scale: clamp(round(x / scale), -8, 7) + 8 with
+// IEEE division; round = half away from zero or half to even (tie mode).
+template <int TIE>
+__device__ __forceinline__ uint32_t code_of(float x, float scale) {
+  float q = __fdiv_rn(x, scale);
+  float r;
+  if (TIE == KV4_TIE_HALF_EVEN) {
+    r = rintf(q);
+  } else {
+    r = (q >= 0.0f) ? floorf(__fadd_rn(q, 0.5f)) : ceilf(__fsub_rn(q, 0.5f));
+  }
+  r = fmaxf(-8.0f, fminf(7.0f, r));
+  return static_cast<uint32_t>(static_cast<int>(r) + 8);
+}
+
 }  // namespace kv4

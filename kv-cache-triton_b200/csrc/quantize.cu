@@ -60,19 +60,6 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *p, flo
   load8_16<__nv_bfloat162>(p, v);
 }
 
-template <int TIE>
-__device__ __forceinline__ uint32_t code_of(float x, float scale) {
-  float q = __fdiv_rn(x, scale);
-  float r;
-  if (TIE == KV4_TIE_HALF_EVEN) {
-    r = rintf(q);
-  } else {
-    r = (q >= 0.0f) ? floorf(__fadd_rn(q, 0.5f)) : ceilf(__fsub_rn(q, 0.5f));
-  }
-  r = fmaxf(-8.0f, fminf(7.0f, r));
-  return static_cast<uint32_t>(static_cast<int>(r) + 8);
-}
-
 template <typename XT, typename ST, int TIE>
 __global__ void __launch_bounds__(256) quantize_kernel(const QParams P) {
   const int64_t per_job = P.rows * P.ng;

@@ -25,7 +25,7 @@ KV4_ERR_SCRATCH_LIMIT = 9
 EXPORTED = (
     "kv4_version", "kv4_strerror", "kv4_last_cuda_error", "kv4_quantize", "kv4_append_kv",
     "kv4_dequantize", "kv4_attention", "kv4_attention_plan", "kv4_attention_partial",
-    "kv4_lse_combine", "kv4_device_error", "kv4_attention_noalloc",
+    "kv4_lse_combine", "kv4_device_error", "kv4_attention_noalloc", "kv4_append_attention",
 )
 
 
@@ -99,6 +99,8 @@ def lib() -> ctypes.CDLL:
     L.kv4_lse_combine.argtypes = [vp, vp, i64, T, vp]
     L.kv4_device_error.argtypes = [vp, P(ctypes.c_int)]
     L.kv4_attention_noalloc.argtypes = [T, T, T, T, T, T, i32, i32, f32, vp]
+    L.kv4_append_attention.argtypes = [T, T, T, T, T, T, T, T, i32, i32, i32, f32, vp, sz,
+                                       P(AttnOpts), vp]
     for name in EXPORTED:
         if name not in ("kv4_version", "kv4_strerror", "kv4_last_cuda_error"):
             getattr(L, name).restype = i32

@@ -81,6 +81,41 @@ class Int4KVStore:
         )
 
     def append(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int) -> None:
+        layer = self._reserve(key_states, value_states, layer_idx)
+        s = key_states.shape[2]
+        if s == 0:
+            return
+        ops.append_kv(key_states, value_states, layer.k_packed_buf, layer.k_scales_buf,
+                      layer.v_packed_buf, layer.v_scales_buf, layer.seq_len, self.group_size,
+                      self.tie_mode)
+        layer.seq_len += s
+
+    def append_attend(self, query: torch.Tensor, key_states: torch.Tensor,
+                      value_states: torch.Tensor, layer_idx: int, out: torch.Tensor, *,
+                      n_q_heads: int, n_kv_heads: int, is_causal: bool = False) -> torch.Tensor:
+        """``append`` followed by attention of ``query`` over the whole layer
+        cache, written to ``out`` (any strides, [B, Hq, sq, d]).  A one-token
+        decode step is a single launch: the attention kernel quantizes the new
+        row itself (``kv4_append_attention``)."""
+        layer = self._reserve(key_states, value_states, layer_idx)
+        s = key_states.shape[2]
+        if s != 1:
+            self.append(key_states, value_states, layer_idx)
+            kp, ks, vp, vs = self.layer(layer_idx).views()
+            return frontend.attention(query, kp, ks, vp, vs, n_q_heads=n_q_heads,
+                                      n_kv_heads=n_kv_heads, group_size=self.group_size,
+                                      is_causal=is_causal, out=out)
+        n = layer.seq_len + 1
+        ops.append_attention_into(query, key_states, value_states,
+                                  layer.k_packed_buf[:, :, :n], layer.k_scales_buf[:, :, :n],
+                                  layer.v_packed_buf[:, :, :n], layer.v_scales_buf[:, :, :n],
+                                  out, self.group_size, is_causal, self.tie_mode)
+        layer.seq_len = n
+        return out
+
+    def _reserve(self, key_states: torch.Tensor, value_states: torch.Tensor,
+                 layer_idx: int) -> LayerStore:
+        """Check the new states and make room for them (valid rows unchanged)."""
         if key_states.shape != value_states.shape or key_states.dim() != 4:
             raise ValueError("key/value states must both be [B, n_kv, s, d_head]")
         if key_states.dtype not in frontend.FLOATS or value_states.dtype != key_states.dtype:
@@ -112,12 +147,7 @@ class Int4KVStore:
                 grown.seq_len = n
                 layer = grown
                 self._layers[layer_idx] = layer
-        if s == 0:
-            return
-        ops.append_kv(key_states, value_states, layer.k_packed_buf, layer.k_scales_buf,
-                      layer.v_packed_buf, layer.v_scales_buf, layer.seq_len, self.group_size,
-                      self.tie_mode)
-        layer.seq_len += s
+        return layer
 
     def layer(self, layer_idx: int) -> LayerStore:
         st = self._layers.get(layer_idx)

@@ -135,6 +135,31 @@ def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = Fa
                           ws.numel() if ws is not None else 0, optr, _stream(q.device)))
 
 
+def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
+                          is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
+                          sm_scale: float = 0.0, **kw) -> None:
+    """Quantize ``k_new``/``v_new`` [B, Hkv, n, d] into the LAST n rows of the
+    cache views ``kp, ks, vp, vs`` (which already span the new rows), then
+    attend over all rows: one launch for n == 1 on the fast path
+    (``kv4_append_attention``)."""
+    L = lib()
+    ds = [desc(t) for t in (q, kp, ks, vp, vs, out)]
+    dn = [desc(t) for t in (k_new, v_new)]
+    o = _opts(**kw)
+    optr = ctypes.byref(o) if o else None
+    p = AttnPlan()
+    check("kv4_attention_plan",
+          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
+                               optr, ctypes.byref(p)))
+    ws = _workspace(q.device, p)
+    check("kv4_append_attention",
+          L.kv4_append_attention(ctypes.byref(ds[0]), ctypes.byref(dn[0]), ctypes.byref(dn[1]),
+                                 *[ctypes.byref(d) for d in ds[1:]], int(group_size),
+                                 int(tie_mode), int(is_causal), float(sm_scale),
+                                 ws.data_ptr() if ws is not None else None,
+                                 ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+
+
 def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, sk_total: int,
                            group_size: int, is_causal: bool = False, sm_scale: float = 0.0,
                            **kw) -> None:

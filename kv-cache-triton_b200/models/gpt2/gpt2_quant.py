@@ -79,8 +79,20 @@ class GPT2AttentionQuantized(GPT2Attention):
         shape_q = (*query_states.shape[:-1], -1, self.head_dim)
         query_states = query_states.view(shape_q).transpose(1, 2)
 
+        # one-token decode on the fused kernel: the append happens inside the
+        # attention launch (QuantizedKVCache.append_attend) below
+        fuse_append = (
+            quant_cache is not None
+            and not is_cross_attention
+            and query_states.is_cuda
+            and query_states.shape[-2] == 1
+            and key_states.shape[-2] == 1
+            and not (self.config._attn_implementation == "eager" and self.reorder_and_upcast_attn)
+            and query_states.dtype in (torch.float16, torch.float32)
+        )
         if quant_cache is not None and not is_cross_attention:
-            quant_cache.append(key_states, value_states, self.layer_idx)
+            if not fuse_append:
+                quant_cache.append(key_states, value_states, self.layer_idx)
         elif (past_key_values is not None and not is_cross_attention) or (
                 past_key_values is not None and is_cross_attention and not is_updated):
             key_states, value_states = curr_past_key_value.update(key_states, value_states,
@@ -109,12 +121,17 @@ class GPT2AttentionQuantized(GPT2Attention):
             attn_output, attn_weights = self._upcast_and_reordered_attn(
                 query_states, key_states, value_states, attention_mask, head_mask)
         elif use_quant_kernel:
-            k_packed, k_scales, v_packed, v_scales = quant_cache.get_quantized(self.layer_idx)
             b, h, sq, d = query_states.shape
             out = torch.empty(b, sq, h, d, dtype=query_states.dtype, device=query_states.device)
-            attention_forward_quant(query_states, k_packed, k_scales, v_packed, v_scales,
-                                    group_size=self.quant_group_size, is_causal=is_causal,
-                                    out=out.transpose(1, 2))
+            if fuse_append:
+                quant_cache.append_attend(query_states, key_states, value_states, self.layer_idx,
+                                          out.transpose(1, 2), n_q_heads=h, n_kv_heads=h,
+                                          is_causal=is_causal)
+            else:
+                k_packed, k_scales, v_packed, v_scales = quant_cache.get_quantized(self.layer_idx)
+                attention_forward_quant(query_states, k_packed, k_scales, v_packed, v_scales,
+                                        group_size=self.quant_group_size, is_causal=is_causal,
+                                        out=out.transpose(1, 2))
             attn_output = out
             attn_weights = None
         else:

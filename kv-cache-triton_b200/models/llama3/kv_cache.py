@@ -75,6 +75,17 @@ class QuantizedKVCache:
         """Quantize ``[B, n_kv, s, d]`` K/V (any strides) into the layer's cache."""
         self._store.append(key_states, value_states, layer_idx)
 
+    def append_attend(self, query: torch.Tensor, key_states: torch.Tensor,
+                      value_states: torch.Tensor, layer_idx: int, out: torch.Tensor, *,
+                      n_q_heads: int, n_kv_heads: int, is_causal: bool = False) -> torch.Tensor:
+        """``append`` then fused attention of ``query`` over the layer's cache
+        into ``out`` ([B, Hq, sq, d], any strides).  One kernel launch for a
+        one-token decode step (the new row is quantized inside the attention
+        kernel); returns ``out``."""
+        return self._store.append_attend(query, key_states, value_states, layer_idx, out,
+                                         n_q_heads=n_q_heads, n_kv_heads=n_kv_heads,
+                                         is_causal=is_causal)
+
     def update(
         self,
         key_states: torch.Tensor,

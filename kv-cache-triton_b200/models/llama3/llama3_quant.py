@@ -11,7 +11,8 @@ dequantized (on the GPU) and the stock HF attention function runs.  Without a
 Differences that keep behaviour but remove copies: the fused kernel reads
 q and the cache views in place (no ``.contiguous()``), and writes its output
 directly in ``[B, s, n_q, d]`` order so the ``o_proj`` input needs no
-transpose copy.
+transpose copy.  A one-token decode step appends and attends in one kernel
+launch (``QuantizedKVCache.append_attend``).
 """
 
 from __future__ import annotations
@@ -59,24 +60,33 @@ class LlamaAttentionQuantized(LlamaAttention):
         quant_cache = past_key_values if isinstance(past_key_values, QuantizedKVCache) else None
 
         if quant_cache is not None:
-            quant_cache.append(key_states, value_states, self.layer_idx)
             n_q = self.config.num_attention_heads
             n_kv = self.config.num_key_value_heads
             sq = query_states.shape[-2]
             is_causal = attention_mask is None and sq > 1
 
             if query_states.is_cuda and attention_mask is None:
-                k_packed, k_scales, v_packed, v_scales = quant_cache.get_quantized(self.layer_idx)
                 b = query_states.shape[0]
                 out = torch.empty(b, sq, n_q, self.head_dim, dtype=query_states.dtype,
                                   device=query_states.device)
-                attention_forward_quant_gqa(
-                    query_states, k_packed, k_scales, v_packed, v_scales,
-                    n_q_heads=n_q, n_kv_heads=n_kv, group_size=self.quant_group_size,
-                    is_causal=is_causal, out=out.transpose(1, 2),
-                )
+                if sq == 1:
+                    # decode: the append is fused into the attention launch
+                    quant_cache.append_attend(query_states, key_states, value_states,
+                                              self.layer_idx, out.transpose(1, 2),
+                                              n_q_heads=n_q, n_kv_heads=n_kv)
+                else:
+                    quant_cache.append(key_states, value_states, self.layer_idx)
+                    k_packed, k_scales, v_packed, v_scales = quant_cache.get_quantized(
+                        self.layer_idx)
+                    attention_forward_quant_gqa(
+                        query_states, k_packed, k_scales, v_packed, v_scales,
+                        n_q_heads=n_q, n_kv_heads=n_kv, group_size=self.quant_group_size,
+                        is_causal=is_causal, out=out.transpose(1, 2),
+                    )
                 attn_output = self.o_proj(out.view(*input_shape, -1))
                 return attn_output, None
+
+            quant_cache.append(key_states, value_states, self.layer_idx)
 
             k_full, v_full = quant_cache.get_dequantized(self.layer_idx,
                                                          out_dtype=query_states.dtype)
