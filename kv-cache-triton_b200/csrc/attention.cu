@@ -27,6 +27,7 @@
 #include <cmath>
 #include <climits>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -246,6 +247,17 @@ __device__ __forceinline__ void st_bytes_shared(uint32_t a, uint32_t w) {
   else if constexpr (NB == 2) asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "r"(w) : "memory");
   else asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(w) : "memory");
 }
+// one scale (bf16 / f16 / f32 in shared memory) as fp32
+template <typename ST>
+__device__ __forceinline__ float lds_scale(uint32_t a) {
+  if constexpr (sizeof(ST) == 2) {
+    const uint32_t w = lds16(a);
+    if constexpr (std::is_same<ST, __nv_bfloat16>::value) return __uint_as_float(w << 16);
+    else return __half2float(__ushort_as_half(static_cast<unsigned short>(w)));
+  } else {
+    return __uint_as_float(lds32(a));
+  }
+}
 template <int NB>
 __device__ __forceinline__ uint32_t ld_bytes_shared(uint32_t a) {
   uint32_t w;
@@ -292,24 +304,17 @@ struct FastCfg {
 
 // Nibble extraction into bf16x2 "128 + code" values (exact; bf16 0x4300|n ==
 // 128 + n).  Each picks the same nibble of bytes k and k+2 of x into the low
-// and high 16-bit halves.  Only the byte-0/2 low nibbles sit in place; the
-// others are moved with mad.hi (x & mask) * 2^s + magic, which runs on the
-// FMA pipe instead of the half-rate integer ALU pipe a shift would use.
-__device__ __forceinline__ uint32_t madhi(uint32_t a, uint32_t b, uint32_t c) {
+// and high 16-bit halves: one shift (except for the nibble already in place)
+// and one LOP3 ((x >> s) & 0x000F000F | magic), 7 integer ops per 8 codes.
+__device__ __forceinline__ uint32_t lop_nib(uint32_t x) {
   uint32_t r;
-  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(0x000F000Fu), "r"(0x43004300u));
+  return r;  // (x & m) | magic
 }
-__device__ __forceinline__ uint32_t nib_lo0(uint32_t x) { return (x & 0x000F000Fu) | 0x43004300u; }
-__device__ __forceinline__ uint32_t nib_hi0(uint32_t x) {
-  return madhi(x & 0x00F000F0u, 1u << 28, 0x43004300u);
-}
-__device__ __forceinline__ uint32_t nib_lo1(uint32_t x) {
-  return madhi(x & 0x0F000F00u, 1u << 24, 0x43004300u);
-}
-__device__ __forceinline__ uint32_t nib_hi1(uint32_t x) {
-  return madhi(x & 0xF000F000u, 1u << 20, 0x43004300u);
-}
+__device__ __forceinline__ uint32_t nib_lo0(uint32_t x) { return lop_nib(x); }
+__device__ __forceinline__ uint32_t nib_hi0(uint32_t x) { return lop_nib(x >> 4); }
+__device__ __forceinline__ uint32_t nib_lo1(uint32_t x) { return lop_nib(x >> 8); }
+__device__ __forceinline__ uint32_t nib_hi1(uint32_t x) { return lop_nib(x >> 12); }
 
 template <int NG, typename ST>
 __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
@@ -727,6 +732,16 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     for (int cp = 0; cp < NCH / 2; ++cp)
       m_off[cp] = r * P_ + 16 * ((2 * cp + (lane >> 4)) ^ key);
   }
+  // K: one x4 load per chunk covers rows g, g+8, 16+g, 24+g (lane L feeds
+  // row L of the warp's 32 rows); the swizzle key of a row depends on
+  // row mod 8 only.
+  uint32_t k_off[NCH];
+  {
+    const int r = WROWS * warp + lane;
+    const int key = (r >> Cfg::SH) & Cfg::SWZ;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) k_off[c] = r * P_ + 16 * (c ^ key);
+  }
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
   load_unit();  // q loads overlap the first TMA loads already in flight
@@ -765,51 +780,52 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       __syncwarp();
     }
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
-    float sc[2][NG][4];  // first MMA of each group takes the bias as its C input
+    // Per scale group: partial dot products on the tensor cores (the first
+    // MMA of a group takes the -136*sum(q) bias as its C input), then the
+    // group's K scale in fp32 into s[h][r][cc] (sub-tile h, row g / g+8,
+    // column 2tg+cc).
+    float s[2][2][2] = {};
 #pragma unroll
-    for (int cp = 0; cp < NCH / 2; ++cp) {
+    for (int gi = 0; gi < NG; ++gi) {
+      float acc[2][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t xr[4];  // x0, x1 of chunk 2cp, then of chunk 2cp+1
-        ldsm_x4(kp + m_off[cp] + h * 16 * P_, xr);
+      for (int cc = 0; cc < CPG; ++cc) {
+        const int c = gi * CPG + cc;
+        uint32_t xr[4];  // rows g, g+8 of sub-tile 0, then of sub-tile 1
+        ldsm_x4(kp + k_off[c], xr);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = 2 * cp + e;
-          const int gi = c / CPG;
-          const uint32_t x0 = xr[2 * e], x1 = xr[2 * e + 1];
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t x0 = xr[2 * h], x1 = xr[2 * h + 1];
           const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
           const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
-          if (c % CPG == 0)
-            mma_bf16_16816_c(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
+          if (cc == 0)
+            mma_bf16_16816_c(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
                              bias[gi][1], bias[gi][0], bias[gi][1]);
           else
-            mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
-          mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
+            mma_bf16_16816(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
+          mma_bf16_16816(acc[h], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
           if constexpr (SPLIT) {
-            mma_bf16_16816(sc[h][gi], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
-            mma_bf16_16816(sc[h][gi], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
+            mma_bf16_16816(acc[h], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
+            mma_bf16_16816(acc[h], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
           }
         }
       }
+      constexpr int SS = static_cast<int>(sizeof(ST));
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const float ks = lds_scale<ST>(ksb + s_row0 + (16 * h + 8 * r) * Cfg::SROW + gi * SS);
+          s[h][r][0] = fmaf(ks, acc[h][2 * r], s[h][r][0]);
+          s[h][r][1] = fmaf(ks, acc[h][2 * r + 1], s[h][r][1]);
+        }
     }
-    // s[h][r][cc]: sub-tile h, row g (r=0) / g+8 (r=1), column 2tg+cc
-    float s[2][2][2];
-    float vsc[2][2][NG];
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        float ks[NG];
-        scales_row<NG, ST>(ksb + s_row0 + (16 * h + 8 * r) * Cfg::SROW, ks);
-        scales_row<NG, ST>(vsb + s_row0 + (16 * h + 8 * r) * Cfg::SROW, vsc[h][r]);
-        float a = 0.f, b2 = 0.f;
-#pragma unroll
-        for (int gi = 0; gi < NG; ++gi) {
-          a = fmaf(ks[gi], sc[h][gi][2 * r], a);
-          b2 = fmaf(ks[gi], sc[h][gi][2 * r + 1], b2);
-        }
-        s[h][r][0] = a * C.scale_log2;
-        s[h][r][1] = b2 * C.scale_log2;
+        s[h][r][0] *= C.scale_log2;
+        s[h][r][1] *= C.scale_log2;
       }
     if (tok0 + WROWS > lim_min) {  // only rows that reach past a key limit need masks
 #pragma unroll
@@ -819,11 +835,22 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
           const int t = tok0 + 16 * h + 8 * r + g;
           if (t >= col_lim[0]) s[h][r][0] = kNegInf;
           if (t >= col_lim[1]) s[h][r][1] = kNegInf;
-          if (t >= C.sk) {  // rows past the cache hold stale smem: keep P * scale finite
+          if (t >= C.sk && tg == 0) {
+            // past the cache end the scale bulk copy (rounded up to 16 bytes)
+            // may have brought in bytes from beyond the view: zero the row's V
+            // scales so that P (= 0) times them stays 0
+            const uint32_t row = vsb + s_row0 + (16 * h + 8 * r) * Cfg::SROW;
 #pragma unroll
-            for (int gi = 0; gi < NG; ++gi) vsc[h][r][gi] = 0.0f;
+            for (int e = 0; e < Cfg::SROW / 2; ++e)
+              asm volatile("st.shared.u16 [%0], %1;" ::"r"(row + 2 * e), "r"(0u) : "memory");
           }
         }
+    }
+    // (the zeroed scale rows are read by other lanes of the warp; the next TMA
+    // into this stage is ordered after the writes by the proxy fence)
+    if (tok0 + WROWS > C.sk) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
     }
     // ---------------- online softmax over 32 rows (lazy rescale) --------
     float mx[2];
@@ -881,8 +908,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       uint32_t pbl[SPLIT ? NG : 1][2];
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        const float a0 = p[h][0][0] * vsc[h][0][gi], a1 = p[h][0][1] * vsc[h][0][gi];
-        const float c0 = p[h][1][0] * vsc[h][1][gi], c1 = p[h][1][1] * vsc[h][1][gi];
+        constexpr int SS = static_cast<int>(sizeof(ST));
+        const float vs0 = lds_scale<ST>(vsb + s_row0 + (16 * h) * Cfg::SROW + gi * SS);
+        const float vs1 = lds_scale<ST>(vsb + s_row0 + (16 * h + 8) * Cfg::SROW + gi * SS);
+        const float a0 = p[h][0][0] * vs0, a1 = p[h][0][1] * vs0;
+        const float c0 = p[h][1][0] * vs1, c1 = p[h][1][1] * vs1;
         const uint32_t u0 = pack_bf16x2(a0, a1);
         const uint32_t u1 = pack_bf16x2(c0, c1);
         pb[gi][0] = movmatrix_trans(u0);
