@@ -168,6 +168,47 @@ int kv4_append_attention(const kv4_tensor *q, const kv4_tensor *k_new, const kv4
                          const kv4_attn_opts *opts, void *stream);
 
 /*
+ * Paged (block-table) INT4 cache, a layout the reference does not have (it
+ * keeps one uniform-length contiguous cache per layer, models/llama3/
+ * kv_cache.py:27); it serves ragged batches.  Pools:
+ * k_pages/v_pages u8 [num_pages, Hkv, page, pw] and
+ * k_scale_pages/v_scale_pages [num_pages, Hkv, page, ng] (page in
+ * {8, 16, 32, 64, 128} tokens, rows contiguous).  Sequence b holds
+ * seq_lens[b] tokens (device int32 [B]); its token t is row t % page of page
+ * block_table[b * block_table_stride + t / page] (device int32).  max_seq_len
+ * (host) bounds every seq_lens[b] and sizes the grid; max_blocks bounds the
+ * block-table row.  q/out as for kv4_attention; is_causal aligns each
+ * sequence's queries to its own last key.  Fast-path shapes only (d in
+ * {64, 128, 256}, G in {32, 64, 128}), else KV4_ERR_UNSUPPORTED.  Page ids
+ * outside the pool are skipped and reported by kv4_device_error (bit 2).
+ */
+int kv4_attention_paged(const kv4_tensor *q, const kv4_tensor *k_pages,
+                        const kv4_tensor *k_scale_pages, const kv4_tensor *v_pages,
+                        const kv4_tensor *v_scale_pages, const int32_t *block_table,
+                        int64_t block_table_stride, int64_t max_blocks, const int32_t *seq_lens,
+                        int64_t max_seq_len, const kv4_tensor *out, int group_size, int is_causal,
+                        float sm_scale, void *workspace, size_t workspace_bytes,
+                        const kv4_attn_opts *opts, void *stream);
+
+/* Plan of kv4_attention_paged (grid, workspace size) for the same shapes. */
+int kv4_attention_paged_plan(const kv4_tensor *q, const kv4_tensor *k_pages,
+                             const kv4_tensor *k_scale_pages, const kv4_tensor *v_pages,
+                             const kv4_tensor *v_scale_pages, int64_t max_blocks,
+                             int64_t max_seq_len, int group_size, const kv4_attn_opts *opts,
+                             kv4_attn_plan *plan);
+
+/*
+ * Quantize-on-append into a paged cache: k, v [B, Hkv, n, d] (float);
+ * row (b, h, i) goes to page slot_mapping[b * n + i] / page, row
+ * slot_mapping[b * n + i] % page of head h (device int32 [B * n]; negative
+ * or out-of-pool slots are skipped).  Same arithmetic as kv4_append_kv.
+ */
+int kv4_append_kv_paged(const kv4_tensor *k, const kv4_tensor *v, const kv4_tensor *k_pages,
+                        const kv4_tensor *k_scale_pages, const kv4_tensor *v_pages,
+                        const kv4_tensor *v_scale_pages, const int32_t *slot_mapping,
+                        int group_size, int tie_mode, void *stream);
+
+/*
  * Sequence-shard partial of kv4_attention (new; the reference has no
  * multi-GPU layer, it relies on accelerate device_map placement,
  * benchmarks/llama3/run_llama3_benchmark.py:115-121).  The cache slice holds

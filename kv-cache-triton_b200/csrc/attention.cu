@@ -207,6 +207,16 @@ struct FastParams {
   int64_t kn_sb, kn_sh, vn_sb, vn_sh;  // elements
   uint8_t *kpw, *vpw;                  // packed caches (bytes)
   int64_t kp_sb, kp_sh, kp_st, vp_sb, vp_sh, vp_st;
+  // Paged layout (page > 0): packed/scale tensors are page pools
+  // [npages, Hkv, page, ...] (ks_sb / vs_sb are then page strides); token t
+  // of sequence b lives in page bt[b * bt_stride + t / page], row t % page;
+  // sequence b holds seq_lens[b] tokens (c.sk is the grid's upper bound).
+  int page;
+  int npages;
+  const int32_t *bt;
+  int64_t bt_stride;
+  const int32_t *seq_lens;
+  int bt_slots;  // shared-memory slots for the CTA's block-table slice
 };
 
 // Quantize one d-wide row with a warp: lane l owns dims [DPL*l, DPL*l + DPL)
@@ -357,7 +367,7 @@ __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
   }
 }
 
-template <int D, int G, typename ST, bool SPLIT>
+template <int D, int G, typename ST, bool SPLIT, bool PAGED>
 __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
                   const __grid_constant__ CUtensorMap tm_vp) {
@@ -392,13 +402,32 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   const int part = static_cast<int>(blockIdx.x) - u * kparts;
   const int t_begin = static_cast<int>(static_cast<int64_t>(part) * P.tpu / kparts);
   const int t_end = static_cast<int>(static_cast<int64_t>(part + 1) * P.tpu / kparts);
-  const int ntiles = t_end - t_begin;
-  if (ntiles <= 0) return;
   const int u_bk = u / P.hc, u_hc = u - u_bk * P.hc;
   const int u_b = u_bk / C.Hkv, u_kvh = u_bk - u_b * C.Hkv;
+  // keys of this unit: c.sk, or (paged) the sequence's own length; a CTA
+  // whose range lies past it streams nothing but still takes part in the merge
+  constexpr bool paged = PAGED;
+  int sk_u = C.sk;
+  if (paged) {
+    const int sl = P.seq_lens[u_b];
+    sk_u = sl < 0 ? 0 : (sl < C.sk ? sl : C.sk);
+  }
+  const int ntiles = max(0, min(t_end, (sk_u + TOK - 1) / TOK) - t_begin);
+  if (ntiles <= 0 && !paged) return;
 
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
+
+  // paged: the CTA's slice of the block table (-1 past the sequence's blocks)
+  int *sh_bt = reinterpret_cast<int *>(app_buf + (Cfg::APP + 15) / 16 * 16);
+  const int ppt = paged ? TOK / P.page : 0;  // pages per tile
+  if (paged) {
+    const int nblk = (sk_u + P.page - 1) / P.page;
+    for (int e = tid; e < ntiles * ppt; e += blockDim.x) {
+      const int blk = t_begin * ppt + e;
+      sh_bt[e] = blk < nblk ? P.bt[u_b * P.bt_stride + blk] : -1;
+    }
+  }
 
   if (tid == 0) {
     sh_abort = 0;
@@ -418,6 +447,35 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     const int s = i % Cfg::STAGES;
     const uint32_t bar = bar_base + 8 * s;
     const uint32_t dst = smem_base + s * Cfg::STAGE;
+    if (paged) {
+      // one TMA box per page and tensor, one bulk copy per page of scales;
+      // pages past the sequence are not loaded, ids outside the pool are
+      // reported through the device error word and skipped
+      int nv = 0;
+      for (int k = 0; k < ppt; ++k) {
+        const int pg = sh_bt[i * ppt + k];
+        nv += (pg >= 0 && pg < P.npages) ? 1 : 0;
+      }
+      const uint32_t pbytes = static_cast<uint32_t>(P.page) * (2 * Cfg::P + 2 * Cfg::SROW);
+      mbar_arrive_expect_tx(bar, nv * pbytes);
+      for (int k = 0; k < ppt; ++k) {
+        const int pg = sh_bt[i * ppt + k];
+        if (pg < 0 || pg >= P.npages) {
+          if (pg >= P.npages || (pg < 0 && t0 + k * P.page < sk_u))
+            atomicOr(&g_device_error, DEV_ERR_BAD_PAGE);
+          continue;
+        }
+        const uint32_t op = static_cast<uint32_t>(k * P.page * Cfg::P);
+        const uint32_t os = static_cast<uint32_t>(k * P.page * Cfg::SROW);
+        tma_load_4d(dst + op, &tm_kp, bar, 0, 0, kvh, pg);
+        tma_load_4d(dst + Cfg::KP + op, &tm_vp, bar, 0, 0, kvh, pg);
+        bulk_load(dst + 2 * Cfg::KP + os, P.ks + pg * P.ks_sb + kvh * P.ks_sh,
+                  P.page * Cfg::SROW, bar);
+        bulk_load(dst + 2 * Cfg::KP + Cfg::KS + os, P.vs + pg * P.vs_sb + kvh * P.vs_sh,
+                  P.page * Cfg::SROW, bar);
+      }
+      return;
+    }
     // packed codes: 2 tiled TMA loads (zero-filled past sk); scales: one bulk
     // copy per tensor of the tile's contiguous rows, rounded up to 16 bytes
     const int rem = min(TOK, C.sk - t0);
@@ -559,7 +617,13 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     for (int j = 0; j < 2; ++j) {
       const int n = hcid * NCOL + 2 * tg + j;
       const int qi = n < P.ncols ? n / C.R : 0;
-      col_lim[j] = n < P.ncols ? static_cast<int>(key_limit(C, qi)) : 0;
+      int64_t lim = sk_u;
+      if (C.causal) {
+        const int64_t total = paged ? sk_u : C.sk_total;
+        lim = total - C.sq + qi + 1 - C.k_offset;
+        lim = lim < sk_u ? lim : sk_u;
+      }
+      col_lim[j] = n < P.ncols ? static_cast<int>(lim) : 0;
       m_run[j] = kNegInf;
       l_run[j] = 0.0f;
     }
@@ -835,7 +899,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
           const int t = tok0 + 16 * h + 8 * r + g;
           if (t >= col_lim[0]) s[h][r][0] = kNegInf;
           if (t >= col_lim[1]) s[h][r][1] = kNegInf;
-          if (t >= C.sk && tg == 0) {
+          if (t >= sk_u && tg == 0) {
             // past the cache end the scale bulk copy (rounded up to 16 bytes)
             // may have brought in bytes from beyond the view: zero the row's V
             // scales so that P (= 0) times them stays 0
@@ -848,7 +912,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     }
     // (the zeroed scale rows are read by other lanes of the warp; the next TMA
     // into this stage is ordered after the writes by the proxy fence)
-    if (tok0 + WROWS > C.sk) {
+    if (tok0 + WROWS > sk_u) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
     }
@@ -1101,15 +1165,15 @@ static bool fast_eligible(const kv4_tensor *q, const kv4_tensor *kp, const kv4_t
   return get_encode() != nullptr;
 }
 
-template <int D, int G, typename ST, bool SPLIT>
+template <int D, int G, typename ST, bool SPLIT, bool PAGED = false>
 static int occupancy_of() {
   static int occ = -1;
   if (occ < 0) {
     using Cfg = FastCfg<D, G, ST>;
-    cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT>,
+    cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT>, 128,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT, PAGED>, 128,
                                                       Cfg::SMEM) != cudaSuccess ||
         o < 1)
       o = 1;
@@ -1209,17 +1273,29 @@ static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int row_bytes, in
 }
 
 
-template <int D, int G, typename ST, bool SPLIT>
+template <int D, int G, typename ST, bool SPLIT, bool PAGED>
 static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
                          cudaStream_t st) {
   using Cfg = FastCfg<D, G, ST>;
   CUtensorMap tkp, tvp;
   int rc;
-  if ((rc = encode_packed(&tkp, kp, Cfg::P, TOK))) return rc;
-  if ((rc = encode_packed(&tvp, vp, Cfg::P, TOK))) return rc;
-  occupancy_of<D, G, ST, SPLIT>();  // sets the smem attribute once
-  kv4_attn_fast<D, G, ST, SPLIT><<<pl.ctas, 128, Cfg::SMEM, st>>>(FP, tkp, tvp);
+  const int box_rows = FP.page > 0 ? FP.page : TOK;  // paged: one box per page
+  if ((rc = encode_packed(&tkp, kp, Cfg::P, box_rows))) return rc;
+  if ((rc = encode_packed(&tvp, vp, Cfg::P, box_rows))) return rc;
+  occupancy_of<D, G, ST, SPLIT, PAGED>();  // sets the smem attribute once
+  int smem = Cfg::SMEM;
+  if (FP.page > 0) {  // room for the block-table slice after the staged append row
+    smem += 16 + FP.bt_slots * 4;
+    static int smem_set = Cfg::SMEM;
+    if (smem > smem_set) {
+      rc = cuda_status(cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      if (rc) return rc;
+      smem_set = smem;
+    }
+  }
+  kv4_attn_fast<D, G, ST, SPLIT, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
   return rc;
@@ -1229,8 +1305,11 @@ template <int D, int G, typename ST>
 static int launch_fast_s(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
                          cudaStream_t st) {
-  return pl.split ? launch_fast_t<D, G, ST, true>(FP, pl, kp, ks, vp, vs, st)
-                  : launch_fast_t<D, G, ST, false>(FP, pl, kp, ks, vp, vs, st);
+  if (FP.page > 0)
+    return pl.split ? launch_fast_t<D, G, ST, true, true>(FP, pl, kp, ks, vp, vs, st)
+                    : launch_fast_t<D, G, ST, false, true>(FP, pl, kp, ks, vp, vs, st);
+  return pl.split ? launch_fast_t<D, G, ST, true, false>(FP, pl, kp, ks, vp, vs, st)
+                  : launch_fast_t<D, G, ST, false, false>(FP, pl, kp, ks, vp, vs, st);
 }
 
 template <typename ST>
@@ -1244,6 +1323,69 @@ static int launch_fast_st(const FastParams &FP, const Plan &pl, const kv4_tensor
       KV4_L(256, 64) KV4_L(256, 128)
 #undef KV4_L
   return KV4_ERR_UNSUPPORTED;
+}
+
+// Paged cache: page pools plus a block table and per-sequence lengths.
+struct PagedJob {
+  const int32_t *bt;
+  int64_t bt_stride, max_blocks;
+  const int32_t *seq_lens;
+  int64_t max_seq_len;
+};
+
+static bool page_size_ok(int64_t p) { return p == 8 || p == 16 || p == 32 || p == 64 || p == 128; }
+
+static int validate_paged(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
+                          const kv4_tensor *vp, const kv4_tensor *vs, int G, const PagedJob &J,
+                          Shape &S) {
+  if (!q || !kp || !ks || !vp || !vs || !J.bt || !J.seq_lens) return KV4_ERR_INVALID;
+  if (G <= 0) return KV4_ERR_INVALID;
+  if (!is_float(q->dtype) || kp->dtype != KV4_U8 || vp->dtype != KV4_U8 || !is_float(ks->dtype) ||
+      ks->dtype != vs->dtype)
+    return KV4_ERR_DTYPE;
+  for (int i = 0; i < 4; ++i) {
+    if (kp->shape[i] != vp->shape[i] || ks->shape[i] != vs->shape[i]) return KV4_ERR_SHAPE;
+    if (i < 3 && kp->shape[i] != ks->shape[i]) return KV4_ERR_SHAPE;
+  }
+  S.B = q->shape[0];
+  S.Hq = q->shape[1];
+  S.sq = q->shape[2];
+  S.d = q->shape[3];
+  S.Hkv = kp->shape[1];
+  S.sk = J.max_seq_len;
+  S.pw = kp->shape[3];
+  S.ng = ks->shape[3];
+  S.G = G;
+  if (S.Hkv <= 0 || S.Hq <= 0 || S.Hq % S.Hkv != 0) return KV4_ERR_INVALID;
+  if (S.pw < (S.d + 1) / 2 || S.ng < (S.d + G - 1) / G) return KV4_ERR_SHAPE;
+  if (!page_size_ok(kp->shape[2])) return KV4_ERR_UNSUPPORTED;
+  if (J.max_seq_len < 1 || J.max_blocks < 1 || J.max_seq_len > J.max_blocks * kp->shape[2] ||
+      J.bt_stride < J.max_blocks)
+    return KV4_ERR_SHAPE;
+  if (kp->shape[0] < 1 || kp->shape[0] > INT_MAX) return KV4_ERR_SHAPE;
+  return KV4_OK;
+}
+
+// Recompute the split-dependent fields of a fast plan for kparts = k.
+static void set_parts(Plan &pl, int64_t k) {
+  k = std::max<int64_t>(1, std::min<int64_t>(k, pl.tpu));
+  pl.maxp = static_cast<int>(k);
+  pl.L = static_cast<int>((pl.tpu + k - 1) / k);
+  pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
+  pl.need_merge = k > 1;
+  pl.ws_bytes = pl.need_merge ? (static_cast<size_t>(pl.units) * sizeof(int) + 15) / 16 * 16 +
+                                    static_cast<size_t>(pl.units) * pl.maxp * NCOL *
+                                        (static_cast<size_t>(pl.D) + 1) * sizeof(float)
+                              : 0;
+}
+
+// paged: keep each CTA's block-table slice within 48 KB of shared memory
+constexpr int kMaxBtBytes = 48 << 10;
+static void paged_plan(Plan &pl, int page) {
+  const int ppt = TOK / page;
+  int64_t k = pl.maxp;
+  while (static_cast<int64_t>((pl.tpu + k - 1) / k) * ppt * 4 > kMaxBtBytes && k < pl.tpu) ++k;
+  if (k != pl.maxp) set_parts(pl, k);
 }
 
 // New tokens appended into the last rows of the cache views before attention.
@@ -1269,10 +1411,11 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
                          const kv4_tensor *lse, int mode, int64_t k_offset, int64_t sk_total,
                          int G, int is_causal, float sm_scale, void *ws, size_t ws_bytes,
                          const kv4_attn_opts *opts, cudaStream_t st,
-                         const AppendJob *app = nullptr) {
+                         const AppendJob *app = nullptr, const PagedJob *pgj = nullptr) {
   Shape S;
-  int rc = validate(q, kp, ks, vp, vs, G, S);
+  int rc = pgj ? validate_paged(q, kp, ks, vp, vs, G, *pgj, S) : validate(q, kp, ks, vp, vs, G, S);
   if (rc) return rc;
+  if (pgj && (app || mode != OUT_FINAL)) return KV4_ERR_UNSUPPORTED;
   if (app && (rc = check_append(*app, S))) return rc;
   if (!out) return KV4_ERR_INVALID;
   for (int i = 0; i < 4; ++i)
@@ -1316,6 +1459,10 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
 
   Plan pl;
   make_plan(q, kp, ks, vp, vs, S, opts, pl);
+  if (pgj) {  // the paged layout runs on the fast path only
+    if (pl.path != 1) return KV4_ERR_UNSUPPORTED;
+    paged_plan(pl, static_cast<int>(kp->shape[2]));
+  }
   // one new token on the fast path is quantized inside the attention launch;
   // anything else is appended by the quantize kernel first (same stream)
   const bool fuse_app = app && pl.path == 1 && app->k->shape[2] == 1 &&
@@ -1329,6 +1476,14 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
   if (pl.path == 1) {
     FastParams FP{};
     FP.app_row = -1;
+    if (pgj) {
+      FP.page = static_cast<int>(kp->shape[2]);
+      FP.npages = static_cast<int>(kp->shape[0]);
+      FP.bt = pgj->bt;
+      FP.bt_stride = pgj->bt_stride;
+      FP.seq_lens = pgj->seq_lens;
+      FP.bt_slots = pl.L * (TOK / FP.page);
+    }
     if (fuse_app) {
       FP.app_row = static_cast<int>(S.sk - 1);
       FP.app_tie = app->tie;
@@ -1424,6 +1579,46 @@ extern "C" int kv4_append_attention(const kv4_tensor *q, const kv4_tensor *k_new
   return run_attention(q, k_packed, k_scales, v_packed, v_scales, out, nullptr, OUT_FINAL, 0, 0,
                        group_size, is_causal, sm_scale, workspace, workspace_bytes, opts,
                        static_cast<cudaStream_t>(stream), &app);
+}
+
+extern "C" int kv4_attention_paged(const kv4_tensor *q, const kv4_tensor *k_pages,
+                                   const kv4_tensor *k_scale_pages, const kv4_tensor *v_pages,
+                                   const kv4_tensor *v_scale_pages, const int32_t *block_table,
+                                   int64_t block_table_stride, int64_t max_blocks,
+                                   const int32_t *seq_lens, int64_t max_seq_len,
+                                   const kv4_tensor *out, int group_size, int is_causal,
+                                   float sm_scale, void *workspace, size_t workspace_bytes,
+                                   const kv4_attn_opts *opts, void *stream) {
+  const PagedJob pj{block_table, block_table_stride, max_blocks, seq_lens, max_seq_len};
+  return run_attention(q, k_pages, k_scale_pages, v_pages, v_scale_pages, out, nullptr, OUT_FINAL,
+                       0, 0, group_size, is_causal, sm_scale, workspace, workspace_bytes, opts,
+                       static_cast<cudaStream_t>(stream), nullptr, &pj);
+}
+
+extern "C" int kv4_attention_paged_plan(const kv4_tensor *q, const kv4_tensor *k_pages,
+                                        const kv4_tensor *k_scale_pages,
+                                        const kv4_tensor *v_pages,
+                                        const kv4_tensor *v_scale_pages, int64_t max_blocks,
+                                        int64_t max_seq_len, int group_size,
+                                        const kv4_attn_opts *opts, kv4_attn_plan *plan) {
+  if (!plan) return KV4_ERR_INVALID;
+  static const int32_t dummy = 0;
+  const PagedJob pj{&dummy, max_blocks, max_blocks, &dummy, max_seq_len};
+  Shape S;
+  int rc = validate_paged(q, k_pages, k_scale_pages, v_pages, v_scale_pages, group_size, pj, S);
+  if (rc) return rc;
+  Plan pl;
+  make_plan(q, k_pages, k_scale_pages, v_pages, v_scale_pages, S, opts, pl);
+  if (pl.path != 1) return KV4_ERR_UNSUPPORTED;
+  paged_plan(pl, static_cast<int>(k_pages->shape[2]));
+  plan->path = pl.path;
+  plan->ctas = pl.ctas;
+  plan->tiles_per_cta = pl.L;
+  plan->units = pl.units;
+  plan->max_parts = pl.maxp;
+  plan->kernels = 1;
+  plan->workspace_bytes = static_cast<int64_t>(pl.ws_bytes);
+  return KV4_OK;
 }
 
 extern "C" int kv4_attention_partial(const kv4_tensor *q, const kv4_tensor *k_packed,

@@ -16,7 +16,7 @@ namespace kv4 {
 void set_cuda_error(cudaError_t e);
 int cuda_status(cudaError_t e);  // KV4_OK or KV4_ERR_CUDA (records the string)
 
-enum DeviceErr : int { DEV_ERR_MBAR_TIMEOUT = 1 };
+enum DeviceErr : int { DEV_ERR_MBAR_TIMEOUT = 1, DEV_ERR_BAD_PAGE = 2 };
 
 // ---------------------------------------------------------------------------
 // scalar conversions

@@ -22,6 +22,11 @@ struct QJob {
   void *s;
   int64_t ss[4];  // scales strides (elements)
   int64_t t_off;  // row offset applied to dim 2 of packed/scales
+  // paged destination (slots != nullptr): row (i0, i1, i2) goes to page
+  // slots[i0 * n2 + i2] / page, row slots[...] % page of head i1 (negative
+  // slots are skipped); dim 0 of packed/scales is then the page
+  const int32_t *slots;
+  int64_t page, npages;  // slots past the pool are skipped as well
 };
 
 struct QParams {
@@ -98,8 +103,16 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QParams P) {
     }
     const float scale = mx > 0.0f ? __fdiv_rn(mx, 7.0f) : 1.0f;
 
+    // destination row: (i0, i1, i2 + t_off), or the paged slot of (i0, i2)
+    int64_t d0 = i0, d2 = i2 + J.t_off;
+    if (J.slots) {
+      const int64_t slot = J.slots[i0 * P.n2 + i2];
+      if (slot < 0 || slot >= J.page * J.npages) continue;
+      d0 = slot / J.page;
+      d2 = slot - d0 * J.page;
+    }
     // pass 2: codes, packed two per byte, emitted 4 bytes at a time
-    uint8_t *prow = J.p + i0 * J.ps[0] + i1 * J.ps[1] + (i2 + J.t_off) * J.ps[2];
+    uint8_t *prow = J.p + d0 * J.ps[0] + i1 * J.ps[1] + d2 * J.ps[2];
     uint8_t *pg = prow + static_cast<int64_t>(grp) * P.pb * J.ps[3];
     const bool pvec = (J.ps[3] == 1) && ((reinterpret_cast<uintptr_t>(pg) & 3) == 0) &&
                       (P.pb % 4 == 0);
@@ -125,7 +138,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QParams P) {
         pg[b * J.ps[3]] = static_cast<uint8_t>(lo | (hi << 4));
       }
     }
-    ST *srow = static_cast<ST *>(J.s) + i0 * J.ss[0] + i1 * J.ss[1] + (i2 + J.t_off) * J.ss[2];
+    ST *srow = static_cast<ST *>(J.s) + d0 * J.ss[0] + i1 * J.ss[1] + d2 * J.ss[2];
     srow[grp * J.ss[3]] = from_f32<ST>(scale);
   }
 }
@@ -286,6 +299,57 @@ extern "C" int kv4_append_kv(const kv4_tensor *k, const kv4_tensor *v,
   if (k->dtype == KV4_F32) launch_quant_x<float>(P, k_scales->dtype, tie_mode, st);
   else if (k->dtype == KV4_F16) launch_quant_x<__half>(P, k_scales->dtype, tie_mode, st);
   else launch_quant_x<__nv_bfloat16>(P, k_scales->dtype, tie_mode, st);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int kv4_append_kv_paged(const kv4_tensor *k, const kv4_tensor *v,
+                                   const kv4_tensor *k_pages, const kv4_tensor *k_scale_pages,
+                                   const kv4_tensor *v_pages, const kv4_tensor *v_scale_pages,
+                                   const int32_t *slot_mapping, int group_size, int tie_mode,
+                                   void *stream) {
+  if (!k || !v || !k_pages || !k_scale_pages || !v_pages || !v_scale_pages || !slot_mapping)
+    return KV4_ERR_INVALID;
+  // shape checks as for a contiguous append of B*n rows into one page
+  // (dims 0 and 2 of the pools are pages and rows, not batch and tokens)
+  for (int i = 0; i < 4; ++i)
+    if (k->shape[i] != v->shape[i]) return KV4_ERR_SHAPE;
+  if (k->dtype != v->dtype || k_scale_pages->dtype != v_scale_pages->dtype) return KV4_ERR_DTYPE;
+  for (int i = 0; i < 4; ++i)
+    if (k_pages->shape[i] != v_pages->shape[i] || k_scale_pages->shape[i] != v_scale_pages->shape[i])
+      return KV4_ERR_SHAPE;
+  if (k_pages->shape[0] != k_scale_pages->shape[0] || k_pages->shape[2] != k_scale_pages->shape[2] ||
+      k_pages->shape[1] != k->shape[1] || k_scale_pages->shape[1] != k->shape[1])
+    return KV4_ERR_SHAPE;
+  if (group_size <= 0) return KV4_ERR_INVALID;
+  if (tie_mode != KV4_TIE_HALF_AWAY && tie_mode != KV4_TIE_HALF_EVEN) return KV4_ERR_INVALID;
+  if (!is_float_dtype(k->dtype) || !is_float_dtype(k_scale_pages->dtype) ||
+      k_pages->dtype != KV4_U8 || v_pages->dtype != KV4_U8)
+    return KV4_ERR_DTYPE;
+  const int64_t d = k->shape[3];
+  const int64_t ng = (d + group_size - 1) / group_size, pb = (group_size + 1) / 2;
+  if (k_pages->shape[3] < ng * pb || k_scale_pages->shape[3] < ng) return KV4_ERR_SHAPE;
+  const int64_t rows = k->shape[0] * k->shape[1] * k->shape[2];
+  if (rows == 0 || d == 0) return KV4_OK;
+  QParams P{};
+  fill_job(P.job[0], k, k_pages, k_scale_pages, 0);
+  fill_job(P.job[1], v, v_pages, v_scale_pages, 0);
+  for (int j = 0; j < 2; ++j) {
+    P.job[j].slots = slot_mapping;
+    P.job[j].page = k_pages->shape[2];
+    P.job[j].npages = k_pages->shape[0];
+  }
+  P.njobs = 2;
+  P.n1 = k->shape[1];
+  P.n2 = k->shape[2];
+  P.rows = rows;
+  P.d = d;
+  P.G = group_size;
+  P.ng = static_cast<int>(ng);
+  P.pb = static_cast<int>(pb);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k->dtype == KV4_F32) launch_quant_x<float>(P, k_scale_pages->dtype, tie_mode, st);
+  else if (k->dtype == KV4_F16) launch_quant_x<__half>(P, k_scale_pages->dtype, tie_mode, st);
+  else launch_quant_x<__nv_bfloat16>(P, k_scale_pages->dtype, tie_mode, st);
   return cuda_status(cudaGetLastError());
 }
 

@@ -18,8 +18,12 @@ _DT = {torch.float32: _lib.KV4_F32, torch.float16: _lib.KV4_F16,
        torch.bfloat16: _lib.KV4_BF16, torch.uint8: _lib.KV4_U8}
 
 
-def desc(t: torch.Tensor) -> Tensor:
-    """kv4_tensor for ``t`` (rank <= 4, leading dims padded with size 1)."""
+def desc(t: torch.Tensor, host_ok: bool = False) -> Tensor:
+    """kv4_tensor for ``t`` (rank <= 4, leading dims padded with size 1).
+    Compute calls take device memory only (``host_ok`` is for the host-only
+    planning calls)."""
+    if not host_ok and not t.is_cuda:
+        raise ValueError("kvint4 kernels take CUDA tensors (no CPU path)")
     n = t.dim()
     if not 1 <= n <= 4:
         raise ValueError("kvint4 tensors have 1 to 4 dims")
@@ -109,7 +113,7 @@ def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0):
 
 def plan(q, kp, ks, vp, vs, out, group_size, is_causal=False, **kw) -> AttnPlan:
     L = lib()
-    ds = [desc(t) for t in (q, kp, ks, vp, vs, out)]
+    ds = [desc(t, host_ok=True) for t in (q, kp, ks, vp, vs, out)]
     o = _opts(**kw)
     p = AttnPlan()
     check("kv4_attention_plan",
@@ -158,6 +162,59 @@ def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
                                  int(tie_mode), int(is_causal), float(sm_scale),
                                  ws.data_ptr() if ws is not None else None,
                                  ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+
+
+def append_kv_paged(k, v, k_pages, ks_pages, v_pages, vs_pages, slot_mapping: torch.Tensor,
+                    group_size: int, tie: int = _lib.TIE_HALF_AWAY) -> None:
+    """Quantize k, v [B, Hkv, n, d] into the page pools at ``slot_mapping``
+    (int32 [B * n] on the device: page * page_size + row; < 0 skips)."""
+    if slot_mapping.dtype != torch.int32 or not slot_mapping.is_contiguous() or \
+            slot_mapping.device != k.device:
+        raise ValueError("slot_mapping must be a contiguous int32 tensor on the device of k")
+    L = lib()
+    ds = [desc(t) for t in (k, v, k_pages, ks_pages, v_pages, vs_pages)]
+    check("kv4_append_kv_paged",
+          L.kv4_append_kv_paged(*[ctypes.byref(d) for d in ds], slot_mapping.data_ptr(),
+                                int(group_size), int(tie), _stream(k.device)))
+
+
+def paged_plan(q, k_pages, ks_pages, v_pages, vs_pages, max_blocks: int, max_seq_len: int,
+               group_size: int, **kw) -> AttnPlan:
+    L = lib()
+    ds = [desc(t, host_ok=True) for t in (q, k_pages, ks_pages, v_pages, vs_pages)]
+    o = _opts(**kw)
+    p = AttnPlan()
+    check("kv4_attention_paged_plan",
+          L.kv4_attention_paged_plan(*[ctypes.byref(d) for d in ds], int(max_blocks),
+                                     int(max_seq_len), int(group_size),
+                                     ctypes.byref(o) if o else None, ctypes.byref(p)))
+    return p
+
+
+def attention_paged_into(q, k_pages, ks_pages, v_pages, vs_pages, block_table: torch.Tensor,
+                         seq_lens: torch.Tensor, max_seq_len: int, out, group_size: int,
+                         is_causal: bool = False, sm_scale: float = 0.0, **kw) -> None:
+    """Attention over a paged INT4 cache (``kv4_attention_paged``):
+    block_table int32 [B, max_blocks], seq_lens int32 [B], both on the device."""
+    for t, name in ((block_table, "block_table"), (seq_lens, "seq_lens")):
+        if t.dtype != torch.int32 or t.device != q.device:
+            raise ValueError(f"{name} must be an int32 tensor on the device of q")
+    if block_table.dim() != 2 or block_table.stride(1) != 1 or not seq_lens.is_contiguous():
+        raise ValueError("block_table must be [B, max_blocks] with unit column stride")
+    L = lib()
+    ds = [desc(t) for t in (q, k_pages, ks_pages, v_pages, vs_pages, out)]
+    p = paged_plan(q, k_pages, ks_pages, v_pages, vs_pages, block_table.shape[1], max_seq_len,
+                   group_size, **kw)
+    ws = _workspace(q.device, p)
+    o = _opts(**kw)
+    check("kv4_attention_paged",
+          L.kv4_attention_paged(*[ctypes.byref(d) for d in ds[:5]], block_table.data_ptr(),
+                                block_table.stride(0), block_table.shape[1], seq_lens.data_ptr(),
+                                int(max_seq_len), ctypes.byref(ds[5]), int(group_size),
+                                int(is_causal), float(sm_scale),
+                                ws.data_ptr() if ws is not None else None,
+                                ws.numel() if ws is not None else 0,
+                                ctypes.byref(o) if o else None, _stream(q.device)))
 
 
 def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, sk_total: int,
