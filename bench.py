@@ -43,6 +43,8 @@ WORKLOADS = {
     "long16k": dict(B=1, HQ=32, HKV=8, S=16384),
     "long64k": dict(B=1, HQ=32, HKV=8, S=65536),
     "long128k": dict(B=1, HQ=32, HKV=8, S=131072),
+    # config 4: Llama-3.1-70B shape with one KV head (and its 8 q heads) per GPU
+    "config4": dict(B=32, HQ=8, HKV=1, S=16384),
 }
 B, HQ, HKV, S, D, G = 16, 32, 8, 4096, 128, 32
 LAYERS = 32
@@ -69,7 +71,8 @@ def set_workload(name):
     B, HQ, HKV, S = w["B"], w["HQ"], w["HKV"], w["S"]
     # enough layer caches to keep ~2.4 GB resident (>> the 126 MB L2)
     LAYERS = max(2, min(32, -(-2_400_000_000 // attn_bytes())))
-    METRIC = (f"INT4-KV decode attention HBM GB/s (Llama-3.1-8B shape, B{B}, S{S}, G{G})")
+    shape = "Llama-3.1-70B shape, 1 KV head/GPU" if name == "config4" else "Llama-3.1-8B shape"
+    METRIC = f"INT4-KV decode attention HBM GB/s ({shape}, B{B}, S{S}, G{G})"
 
 
 def _dist():
@@ -330,7 +333,7 @@ def run_ours(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
         "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
-        "config": {"workload": f"{args.workload}: llama3.1-8b single-layer decode: append 1 "
+        "config": {"workload": f"{args.workload}: {"llama3.1-70b" if args.workload == "config4" else "llama3.1-8b"} single-layer decode: append 1 "
                                "token + INT4 decode attention, one fused launch", "batch": B, "q_heads": HQ, "kv_heads": HKV,
                    "seq_len": S, "d_head": D, "group_size": G,
                    "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
