@@ -149,6 +149,20 @@ class Int4KVStore:
                 self._layers[layer_idx] = layer
         return layer
 
+    def crop(self, max_length: int) -> None:
+        """Keep the first ``max_length`` tokens of every layer (negative: drop
+        that many from the end), as ``DynamicCache.crop``."""
+        for st in self._layers.values():
+            n = max_length if max_length >= 0 else st.seq_len + max_length
+            st.seq_len = max(0, min(st.seq_len, n))
+
+    def reorder(self, beam_idx: torch.Tensor) -> None:
+        """Reorder the batch dimension of every layer (beam search)."""
+        for st in self._layers.values():
+            idx = beam_idx.to(st.k_packed_buf.device)
+            for name in ("k_packed_buf", "k_scales_buf", "v_packed_buf", "v_scales_buf"):
+                setattr(st, name, getattr(st, name).index_select(0, idx).contiguous())
+
     def layer(self, layer_idx: int) -> LayerStore:
         st = self._layers.get(layer_idx)
         if st is None:

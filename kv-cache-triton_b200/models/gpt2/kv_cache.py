@@ -59,6 +59,17 @@ class QuantizedKVCache:
     def reset(self) -> None:
         self._layers.clear()
 
+    # HF generate() asks these of any cache object it is given
+    is_compileable = False
+
+    def crop(self, max_length: int) -> None:
+        """Drop tokens past ``max_length`` (negative: that many from the end)."""
+        self._store.crop(max_length)
+
+    def reorder_cache(self, beam_idx: torch.LongTensor) -> None:
+        """Reorder the batch dimension for beam search."""
+        self._store.reorder(beam_idx)
+
     def has_layer(self, layer_idx: int) -> bool:
         return layer_idx in self._layers
 

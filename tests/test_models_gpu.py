@@ -131,3 +131,53 @@ def test_gpt2_random_decode_matches_dynamic_cache():
             o_q = qm(input_ids=nxt, past_key_values=c_q, use_cache=True)
             assert (o_ref.logits[:, -1] - o_q.logits[:, -1]).abs().max().item() < 2.0
     assert c_q.get_seq_length(0) == 26
+
+
+def test_llama_hf_generate_accepts_quantized_cache():
+    """model.generate() threads the INT4 cache through prefill and decode
+    (the reference's scripts/llama3_smoke.py:110-130 does the same); greedy
+    output agrees with the same model on DynamicCache for >= 4 tokens and
+    the cache ends at prompt + new tokens - 1 rows."""
+    from models.llama3.kv_cache import QuantizedKVCache
+    from models.llama3.llama3_quant import replace_llama_attention_with_quantized
+    dev = torch.device("cuda")
+    model_ref = _tiny_llama(dev)
+    model_q = _tiny_llama(dev)
+    model_q.load_state_dict(model_ref.state_dict())
+    replace_llama_attention_with_quantized(model_q, group_size=32)
+    torch.manual_seed(321)
+    prompt = torch.randint(0, 256, (2, 24), device=dev, dtype=torch.long)
+    mask = torch.ones_like(prompt)
+    with torch.inference_mode():
+        a = model_ref.generate(input_ids=prompt, attention_mask=mask, max_new_tokens=12,
+                               do_sample=False, past_key_values=DynamicCache())
+        cache = QuantizedKVCache(group_size=32)
+        b = model_q.generate(input_ids=prompt, attention_mask=mask, max_new_tokens=12,
+                             do_sample=False, past_key_values=cache)
+    assert b.shape == a.shape == (2, 36)
+    assert torch.equal(a[:, :24], b[:, :24])
+    assert torch.equal(a[:, 24], b[:, 24]), (a[:, 24:], b[:, 24:])
+    assert cache.get_seq_length(0) == 24 + 12 - 1
+
+
+def test_gpt2_hf_generate_accepts_quantized_cache():
+    from models.gpt2.gpt2_quant import replace_gpt2_attention_with_quantized
+    from models.gpt2.kv_cache import QuantizedKVCache
+    dev = torch.device("cuda")
+    cfg = GPT2Config(vocab_size=256, n_positions=256, n_embd=128, n_layer=2, n_head=2)
+    torch.manual_seed(0)
+    ref = GPT2LMHeadModel(cfg).to(dev).eval()
+    qm = GPT2LMHeadModel(cfg).to(dev).eval()
+    qm.load_state_dict(ref.state_dict())
+    replace_gpt2_attention_with_quantized(qm, group_size=32)
+    prompt = torch.randint(0, 256, (2, 20), device=dev)
+    mask = torch.ones_like(prompt)
+    with torch.inference_mode():
+        a = ref.generate(input_ids=prompt, attention_mask=mask, max_new_tokens=10,
+                         do_sample=False, past_key_values=DynamicCache())
+        cache = QuantizedKVCache(group_size=32)
+        b = qm.generate(input_ids=prompt, attention_mask=mask, max_new_tokens=10,
+                        do_sample=False, past_key_values=cache)
+    assert b.shape == a.shape == (2, 30)
+    assert torch.equal(a[:, :21], b[:, :21]), (a[:, 20:], b[:, 20:])
+    assert cache.get_seq_length(0) == 29
