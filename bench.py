@@ -436,6 +436,112 @@ def run_reference(args, ws, rank):
     }
 
 
+def run_seq_shard(args, ws, rank, local):
+    """Config 3 across ranks: rank r holds tokens shard_range(S, ws, r) of
+    every layer's batch-1 cache; a step is the partial attention over the
+    local tokens, an NCCL all-gather of (o, lse) and the log-sum-exp combine
+    (kvint4/shard.py).  Total work is fixed as ws grows (strong scaling)."""
+    import torch.distributed as dist
+
+    from kvint4 import ops, shard
+    from kvint4.cache import Int4KVStore
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    lo, hi = shard.shard_range(S, ws, rank)
+    n = hi - lo
+    layers = max(2, min(32, -(-2_400_000_000 // max(1, attn_bytes() // ws))))
+    g = torch.Generator(device=dev).manual_seed(rank)
+    store = Int4KVStore(G, capacity=n)
+    for layer in range(layers):
+        k = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, HKV, n, D, device=dev, generator=g).to(torch.bfloat16)
+        store.append(k, v, layer)
+        del k, v
+    q = torch.randn(layers, B, HQ, 1, D, device=dev,
+                    generator=torch.Generator(device=dev).manual_seed(123)).to(torch.bfloat16)
+    out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def step(l):
+        kp, ks, vp, vs = store.layer(l).views()
+        if ws == 1:
+            ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
+        else:
+            shard.seq_sharded_attention(q[l], kp, ks, vp, vs, k_offset=lo, sk_total=S,
+                                        group_size=G, out=out)
+
+    for l in range(layers):
+        step(l)
+    torch.cuda.synchronize()
+    graph = None
+    try:  # one graph per token: every layer's step (NCCL collectives included)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for l in range(layers):
+                step(l)
+        graph.replay()
+        torch.cuda.synchronize()
+    except Exception:  # eager launches if this NCCL build cannot be captured
+        graph = None
+        torch.cuda.synchronize()
+
+    def run_steps(k):
+        if graph is not None:
+            for _ in range(k // layers):
+                graph.replay()
+            for i in range(k % layers):
+                step(i)
+        else:
+            for i in range(k):
+                step(i % layers)
+
+    run_steps(args.warmup)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(st)
+        run_steps(args.steps)
+        t1.record(st)
+        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    if ws > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if ws > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    peak, peak_kind = _peaks()
+    value = attn_bytes() * args.steps / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "us_per_step": round(ms * 1e3 / args.steps, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": f"{args.workload}: batch-1 decode attention, sequence sharded",
+                   "batch": B, "q_heads": HQ, "kv_heads": HKV, "seq_len": S, "d_head": D,
+                   "group_size": G, "tokens_per_rank": n,
+                   "parallelism": f"sequence shard x{ws}: partial attention + NCCL all-gather "
+                                  "of (o, lse) + LSE combine",
+                   "graph": graph is not None,
+                   "l2": f"steps rotate over {layers} layer caches per rank"},
+        "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / ws, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(value / ws / peak, 4),
+                     "peak_source": peak_kind},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps * (1 if ws == 1 else 2),  # partial + combine per rank
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -444,6 +550,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--shard", choices=["batch", "seq"], default="batch",
+                    help="seq: config-3 sequence sharding over the ranks (strong scaling)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
                     help="config2 = BASELINE config 2 (the headline); long* = config 3")
     args = ap.parse_args()
@@ -453,10 +561,11 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, ws, rank)
     else:
-        line = run_ours(args, ws, rank, local)
+        line = (run_seq_shard(args, ws, rank, local) if args.shard == "seq"
+                else run_ours(args, ws, rank, local))
     if line is not None:
         print(json.dumps(line), flush=True)
-    if ws > 1 and args.impl == "ours":
+    if ws > 1 and args.impl == "ours" and args.shard != "seq":
         torch.distributed.destroy_process_group()
 
 

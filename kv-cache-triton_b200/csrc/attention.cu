@@ -6,18 +6,22 @@
 // and (is_causal) keys j <= sk - sq + i visible (bottom-right alignment).
 //
 // Two device paths:
-//  * fast (kv4_attn_fast): one CTA = 4 warps streams 64-token tiles of packed
-//    K/V + scales from HBM into shared memory with TMA (cp.async.bulk.tensor,
-//    64B/128B/32B swizzle, no multicast), several stages deep.  All q heads of
-//    a GQA group (and all query rows, up to 8 columns per CTA) share ONE read
-//    of the group's KV.  Scores and P.V run on the tensor cores
+//  * fast (kv4_attn_fast): one CTA = 4 warps streams 128-token tiles of
+//    packed K/V + scales from HBM into shared memory (packed rows by 4-D TMA
+//    boxes with the hardware swizzle of the row width, scales by 1-D bulk
+//    copies; no multicast), two stages: "full" mbarriers signal a landed
+//    tile, and the last warp done with a stage refills it.  All q heads
+//    of a GQA group (and all query rows, up to 8 columns per CTA) share ONE
+//    read of the group's KV.  Scores and P.V run on the tensor cores
 //    (mma.m16n8k16 bf16 -> fp32) with the packed nibbles turned into bf16
-//    operands in registers; per-group scales are applied exactly in fp32
-//    (K: after a per-group partial dot product; V: folded into P).  The grid
-//    is persistent and stream-K balanced over (unit, token tile) work;
-//    units split across CTAs leave (o, lse) partials in the workspace, and
-//    the last CTA to finish a unit (per-unit counter) merges them with a
-//    log-sum-exp reduction -- one launch per call.
+//    "128 + code" operands in registers; per-group scales are applied
+//    exactly in fp32 (K: after each group's partial dot product; V: folded
+//    into P).  Split-K: each work unit (batch, KV head, column chunk) is cut
+//    into equal token ranges, one CTA each, sized to one wave of resident
+//    CTAs; the last CTA to finish a unit (per-unit counter) merges the
+//    (o, lse) partials with a log-sum-exp -- one launch per call.  Variants:
+//    the new token's quantize-on-append fused in (kv4_append_attention) and
+//    a paged cache read through a block table (kv4_attention_paged).
 //  * generic (kv4_attn_generic): a warp-per-token FFMA kernel for any shape,
 //    dtype, stride, group size and long query blocks.
 #include <cuda.h>
@@ -307,8 +311,9 @@ struct FastCfg {
   static constexpr int MERGE = NWARP * NCOL * D * 4;
   static_assert(MERGE <= STAGES * STAGE, "merge buffer aliases the stages");
   static constexpr int APP = 2 * P + 2 * SROW;  // staged new row (fused append)
+  static constexpr int BIAS = NWARP * NG * 4 * 16;  // per warp: [group][tg] C quads
   static constexpr int SMEM = STAGES * STAGE + 3 * NWARP * NCOL * 4 + 2 * NCOL * 4 +
-                              16 * STAGES + APP + 1024;
+                              16 * STAGES + (APP + 15) / 16 * 16 + BIAS + 1024;
   static constexpr uint32_t TX = 2 * KP + 2 * KS;
 };
 
@@ -385,11 +390,12 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   float *merge_l = merge_m + NWARP * NCOL;
   float *merge_f = merge_l + NWARP * NCOL;
   float *merge_lse = merge_f + NWARP * NCOL;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(merge_lse + 2 * NCOL);  // full[S], empty[S]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(merge_lse + 2 * NCOL);  // full[S] (+ spare)
   // fused append: quantized new row [K codes P][V codes P][K scales][V scales]
   uint8_t *app_buf = reinterpret_cast<uint8_t *>(bars + 2 * Cfg::STAGES);
   __shared__ int sh_abort;
   __shared__ int sh_last;
+  __shared__ uint32_t sh_done[Cfg::STAGES];  // warps finished with each stage
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -418,8 +424,12 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
 
+  // per warp, per scale group and lane quad tg: the C quad (b0, b1, b0, b1)
+  // that starts the group's score accumulators, b = -136 * sum(q) over the
+  // group for columns 2tg, 2tg+1 (loaded as one 16-byte vector per use)
+  const uint32_t bias_s = smem_u32(app_buf + (Cfg::APP + 15) / 16 * 16);
   // paged: the CTA's slice of the block table (-1 past the sequence's blocks)
-  int *sh_bt = reinterpret_cast<int *>(app_buf + (Cfg::APP + 15) / 16 * 16);
+  int *sh_bt = reinterpret_cast<int *>(app_buf + (Cfg::APP + 15) / 16 * 16 + Cfg::BIAS);
   const int ppt = paged ? TOK / P.page : 0;  // pages per tile
   if (paged) {
     const int nblk = (sk_u + P.page - 1) / P.page;
@@ -429,13 +439,13 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     }
   }
 
+  if (tid < Cfg::STAGES) sh_done[tid] = 0;
   if (tid == 0) {
     sh_abort = 0;
     prefetch_tmap(&tm_kp);
     prefetch_tmap(&tm_vp);
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(bar_base + 8 * s, 1);                            // full: producer + tx
-      mbar_init(bar_base + 8 * (Cfg::STAGES + s), NWARP);        // empty: one per warp
     }
     fence_mbar_init();
   }
@@ -541,7 +551,6 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   // ---- per-unit state --------------------------------------------------
   uint32_t qf[NCH][2][2];               // q B-fragments (hi), [chunk][kstep][reg]
   uint32_t qfl[SPLIT ? NCH : 1][2][2];  // lo parts (SPLIT only)
-  float bias[NG][2];                    // -136 * sum(q) per group for cols 2tg, 2tg+1
   float o_acc[NCH][2][4];               // O^T fragments [chunk][j][c]
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
@@ -609,8 +618,13 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
       for (int gi = 0; gi < NG; ++gi) {
         const float s0 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg) * 4);
         const float s1 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg + 1) * 4);
-        bias[gi][0] = -136.0f * s0;
-        bias[gi][1] = -136.0f * s1;
+        if (g == 0) {
+          const float b0 = -136.0f * s0, b1 = -136.0f * s1;
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %1, %2};" ::"r"(
+                           bias_s + ((warp * NG + gi) * 4 + tg) * 16),
+                       "f"(b0), "f"(b1)
+                       : "memory");
+        }
       }
     }
 #pragma unroll
@@ -809,6 +823,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
   load_unit();  // q loads overlap the first TMA loads already in flight
+  __syncwarp();  // the bias quads written by lanes g == 0 are read by the whole warp
   int stage = -1;
   uint32_t phase = 1;
   for (int i = 0; i < ntiles; ++i) {
@@ -862,10 +877,14 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
           const uint32_t x0 = xr[2 * h], x1 = xr[2 * h + 1];
           const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
           const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
-          if (cc == 0)
-            mma_bf16_16816_c(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bias[gi][0],
-                             bias[gi][1], bias[gi][0], bias[gi][1]);
-          else
+          if (cc == 0) {
+            float bq[4];
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(bq[0]), "=f"(bq[1]), "=f"(bq[2]), "=f"(bq[3])
+                         : "r"(bias_s + ((warp * NG + gi) * 4 + tg) * 16));
+            mma_bf16_16816_c(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bq[0], bq[1],
+                             bq[2], bq[3]);
+          } else
             mma_bf16_16816(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
           mma_bf16_16816(acc[h], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
           if constexpr (SPLIT) {
@@ -1018,17 +1037,20 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : (SPLIT ? 3 : 4)))
     }
 
     // ---------------- release the stage, refill, flush at unit end ------
-    // Each warp frees the stage on its "empty" barrier; thread 0 refills it
-    // once all four warps are done, so warps are not locked in step.
+    // Each warp counts itself out of the stage (acq_rel: its reads of the
+    // stage happen before); the LAST warp to finish refills it at once, so
+    // no warp ever waits for the others.  Counters only grow: the last
+    // arrival of round r of a stage sees NWARP * (r + 1) - 1.
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar_base + 8 * (Cfg::STAGES + stage));
-    if (tid == 0 && i + Cfg::STAGES < ntiles) {
-      if (!*reinterpret_cast<volatile int *>(&sh_abort) &&
-          !mbar_wait_bounded(bar_base + 8 * (Cfg::STAGES + stage), phase)) {
-        atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
-        sh_abort = 1;
-      }
-      issue(i + Cfg::STAGES);
+    if (lane == 0) {
+      uint32_t old;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                   : "=r"(old)
+                   : "r"(smem_u32(&sh_done[stage]))
+                   : "memory");
+      if (old == static_cast<uint32_t>(NWARP * (i / Cfg::STAGES + 1) - 1) &&
+          i + Cfg::STAGES < ntiles)
+        issue(i + Cfg::STAGES);
     }
   }
   flush();
