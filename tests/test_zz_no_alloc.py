@@ -41,7 +41,7 @@ def _noalloc(q, cache, out, gs, causal=False):
 @pytest.mark.parametrize("order", [0, 1])
 def test_noalloc_matches_workspace_entry_point_two_calls(order):
     from kvint4 import ops
-    shapes = [(2, 8, 2, 3000, 128, 32, 1), (3, 32, 8, 700, 128, 64, 2)]
+    shapes = [(2, 8, 2, 3000, 128, 32, 1), (3, 32, 8, 2000, 128, 64, 2)]
     if order:
         shapes = shapes[::-1]
     for (b, hq, hkv, s, d, gs, seed) in shapes:  # two calls in a row, different geometry
