@@ -30,6 +30,8 @@
 #include <algorithm>
 #include <cmath>
 #include <climits>
+#include <atomic>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -1204,11 +1206,16 @@ static int occupancy_of() {
   return occ;
 }
 
-static int sm_count() {
+static int sm_count() {  // per device, queried once
+  static std::atomic<int> cache[64];
   int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return n;
+  if (dev >= 0 && dev < 64 && (n = cache[dev].load(std::memory_order_relaxed)) > 0) return n;
+  n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 template <int D, int G, typename ST, bool SPLIT, typename F>
@@ -1299,6 +1306,42 @@ static int encode_packed(CUtensorMap *tm, const kv4_tensor *t, int row_bytes, in
 }
 
 
+// The last few encoded maps, keyed by everything the encoding reads: a decode
+// loop calls with the same cache views again and again, and encoding is a
+// driver call on every launch otherwise.
+static int encode_packed_cached(CUtensorMap *tm, const kv4_tensor *t, int row_bytes, int tokens) {
+  struct Entry {
+    const void *data;
+    int64_t shape[4], stride[4];
+    int row_bytes, tokens;
+    CUtensorMap map;
+    bool used;
+  };
+  static Entry ring[16];
+  static int next = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (Entry &e : ring)
+    if (e.used && e.data == t->data && e.row_bytes == row_bytes && e.tokens == tokens &&
+        std::memcmp(e.shape, t->shape, sizeof(e.shape)) == 0 &&
+        std::memcmp(e.stride, t->stride, sizeof(e.stride)) == 0) {
+      *tm = e.map;
+      return KV4_OK;
+    }
+  const int rc = encode_packed(tm, t, row_bytes, tokens);
+  if (rc) return rc;
+  Entry &e = ring[next];
+  next = (next + 1) % 16;
+  e.data = t->data;
+  std::memcpy(e.shape, t->shape, sizeof(e.shape));
+  std::memcpy(e.stride, t->stride, sizeof(e.stride));
+  e.row_bytes = row_bytes;
+  e.tokens = tokens;
+  e.map = *tm;
+  e.used = true;
+  return KV4_OK;
+}
+
 template <int D, int G, typename ST, bool SPLIT, bool PAGED>
 static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
@@ -1307,8 +1350,8 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
   CUtensorMap tkp, tvp;
   int rc;
   const int box_rows = FP.page > 0 ? FP.page : TOK;  // paged: one box per page
-  if ((rc = encode_packed(&tkp, kp, Cfg::P, box_rows))) return rc;
-  if ((rc = encode_packed(&tvp, vp, Cfg::P, box_rows))) return rc;
+  if ((rc = encode_packed_cached(&tkp, kp, Cfg::P, box_rows))) return rc;
+  if ((rc = encode_packed_cached(&tvp, vp, Cfg::P, box_rows))) return rc;
   occupancy_of<D, G, ST, SPLIT, PAGED>();  // sets the smem attribute once
   int smem = Cfg::SMEM;
   if (FP.page > 0) {  // room for the block-table slice after the staged append row

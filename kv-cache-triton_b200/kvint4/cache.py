@@ -44,6 +44,18 @@ class LayerStore:
     def capacity(self) -> int:
         return self.k_packed_buf.shape[2]
 
+    def view_descs(self, n: int):
+        """C-ABI descriptors of the four views ``[:, :, :n]``, built from
+        descriptors of the buffers kept on the layer (no torch views)."""
+        bufs = (self.k_packed_buf, self.k_scales_buf, self.v_packed_buf, self.v_scales_buf)
+        cached = getattr(self, "_descs", None)
+        if cached is None or cached[0] != tuple(b.data_ptr() for b in bufs):
+            cached = (tuple(b.data_ptr() for b in bufs), [ops.desc(b) for b in bufs])
+            self._descs = cached
+        for d in cached[1]:
+            d.shape[2] = n
+        return cached[1]
+
     def views(self):
         s = self.seq_len
         return (self.k_packed_buf[:, :, :s], self.k_scales_buf[:, :, :s],
@@ -106,10 +118,8 @@ class Int4KVStore:
                                       n_kv_heads=n_kv_heads, group_size=self.group_size,
                                       is_causal=is_causal, out=out)
         n = layer.seq_len + 1
-        ops.append_attention_into(query, key_states, value_states,
-                                  layer.k_packed_buf[:, :, :n], layer.k_scales_buf[:, :, :n],
-                                  layer.v_packed_buf[:, :, :n], layer.v_scales_buf[:, :, :n],
-                                  out, self.group_size, is_causal, self.tie_mode)
+        ops.append_attention_descs(query, key_states, value_states, layer.view_descs(n), out,
+                                   self.group_size, is_causal, self.tie_mode)
         layer.seq_len = n
         return out
 

@@ -18,6 +18,9 @@ _DT = {torch.float32: _lib.KV4_F32, torch.float16: _lib.KV4_F16,
        torch.bfloat16: _lib.KV4_BF16, torch.uint8: _lib.KV4_U8}
 
 
+_I64x4 = ctypes.c_int64 * 4
+
+
 def desc(t: torch.Tensor, host_ok: bool = False) -> Tensor:
     """kv4_tensor for ``t`` (rank <= 4, leading dims padded with size 1).
     Compute calls take device memory only (``host_ok`` is for the host-only
@@ -25,6 +28,8 @@ def desc(t: torch.Tensor, host_ok: bool = False) -> Tensor:
     if not host_ok and not t.is_cuda:
         raise ValueError("kvint4 kernels take CUDA tensors (no CPU path)")
     n = t.dim()
+    if n == 4:  # the common case, in one constructor call
+        return Tensor(t.data_ptr(), _DT[t.dtype], 0, _I64x4(*t.shape), _I64x4(*t.stride()))
     if not 1 <= n <= 4:
         raise ValueError("kvint4 tensors have 1 to 4 dims")
     shape = [1] * (4 - n) + list(t.shape)
@@ -41,7 +46,9 @@ def desc(t: torch.Tensor, host_ok: bool = False) -> Tensor:
 
 
 def _stream(dev: torch.device) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
+    """Raw handle of the current stream of ``dev`` (no Stream object built)."""
+    return torch._C._cuda_getCurrentRawStream(
+        dev.index if dev.index is not None else torch.cuda.current_device())
 
 
 def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, group_size: int,
@@ -128,15 +135,53 @@ def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = Fa
     ds = [desc(t) for t in (q, kp, ks, vp, vs, out)]
     o = _opts(**kw)
     optr = ctypes.byref(o) if o else None
-    p = AttnPlan()
-    check("kv4_attention_plan",
-          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
-                               optr, ctypes.byref(p)))
-    ws = _workspace(q.device, p)
-    check("kv4_attention",
-          L.kv4_attention(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
-                          float(sm_scale), ws.data_ptr() if ws is not None else None,
-                          ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+    refs = [ctypes.byref(d) for d in ds]
+    st = _stream(q.device)
+
+    def call(ws, nbytes):
+        return L.kv4_attention(*refs, int(group_size), int(is_causal), float(sm_scale), ws,
+                               nbytes, optr, st)
+
+    check("kv4_attention", _with_workspace(q.device, call, ds, group_size, is_causal, optr))
+
+
+def _with_workspace(dev: torch.device, call, ds, group_size, is_causal, optr) -> int:
+    """Run ``call(ws_ptr, ws_bytes)`` with this (device, stream)'s workspace.
+    The common case plans nothing: the library reports KV4_ERR_WORKSPACE
+    (before launching anything) when the buffer is too small, and then the
+    plan sizes a larger one and the call is repeated."""
+    buf = _WS.get((dev.index, _stream(dev)), (None, 0))[0]
+    rc = call(buf.data_ptr() if buf is not None else None, buf.numel() if buf is not None else 0)
+    if rc == _lib.KV4_ERR_WORKSPACE:
+        L = lib()
+        p = AttnPlan()
+        check("kv4_attention_plan",
+              L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size),
+                                   int(is_causal), optr, ctypes.byref(p)))
+        buf = _workspace(dev, p)
+        rc = call(buf.data_ptr() if buf is not None else None,
+                  buf.numel() if buf is not None else 0)
+    return rc
+
+
+def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
+                           is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
+                           sm_scale: float = 0.0) -> None:
+    """``append_attention_into`` with prebuilt descriptors of the four cache
+    views (a decode loop keeps them per layer and only updates the length)."""
+    L = lib()
+    dq, dkn, dvn, do = desc(q), desc(k_new), desc(v_new), desc(out)
+    ds = [dq, *cache_descs, do]
+    refs = [ctypes.byref(d) for d in ds]
+    st = _stream(q.device)
+
+    def call(ws, nbytes):
+        return L.kv4_append_attention(refs[0], ctypes.byref(dkn), ctypes.byref(dvn), *refs[1:],
+                                      int(group_size), int(tie_mode), int(is_causal),
+                                      float(sm_scale), ws, nbytes, None, st)
+
+    check("kv4_append_attention",
+          _with_workspace(q.device, call, ds, group_size, is_causal, None))
 
 
 def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
@@ -151,17 +196,16 @@ def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
     dn = [desc(t) for t in (k_new, v_new)]
     o = _opts(**kw)
     optr = ctypes.byref(o) if o else None
-    p = AttnPlan()
-    check("kv4_attention_plan",
-          L.kv4_attention_plan(*[ctypes.byref(d) for d in ds], int(group_size), int(is_causal),
-                               optr, ctypes.byref(p)))
-    ws = _workspace(q.device, p)
+    refs = [ctypes.byref(d) for d in ds]
+    st = _stream(q.device)
+
+    def call(ws, nbytes):
+        return L.kv4_append_attention(refs[0], ctypes.byref(dn[0]), ctypes.byref(dn[1]),
+                                      *refs[1:], int(group_size), int(tie_mode), int(is_causal),
+                                      float(sm_scale), ws, nbytes, optr, st)
+
     check("kv4_append_attention",
-          L.kv4_append_attention(ctypes.byref(ds[0]), ctypes.byref(dn[0]), ctypes.byref(dn[1]),
-                                 *[ctypes.byref(d) for d in ds[1:]], int(group_size),
-                                 int(tie_mode), int(is_causal), float(sm_scale),
-                                 ws.data_ptr() if ws is not None else None,
-                                 ws.numel() if ws is not None else 0, optr, _stream(q.device)))
+          _with_workspace(q.device, call, ds, group_size, is_causal, optr))
 
 
 def append_kv_paged(k, v, k_pages, ks_pages, v_pages, vs_pages, slot_mapping: torch.Tensor,
