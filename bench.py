@@ -445,8 +445,9 @@ def run_seq_shard(args, ws, rank, local):
     from kvint4.cache import Int4KVStore
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if ws > 1:
-        dist.init_process_group("nccl", device_id=dev)
+    if ws > 1:  # a short timeout: a rank that stops answering ends the run with an error
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
     lo, hi = shard.shard_range(S, ws, rank)
     n = hi - lo
     layers = max(2, min(32, -(-2_400_000_000 // max(1, attn_bytes() // ws))))
@@ -473,16 +474,16 @@ def run_seq_shard(args, ws, rank, local):
     for l in range(layers):
         step(l)
     torch.cuda.synchronize()
+    # Eager launches: the collectives are not captured in a CUDA graph (a
+    # capture that fails on one rank only would leave the ranks' collective
+    # sequences mismatched).  With one GPU the step is a plain attention call.
     graph = None
-    try:  # one graph per token: every layer's step (NCCL collectives included)
+    if ws == 1:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             for l in range(layers):
                 step(l)
         graph.replay()
-        torch.cuda.synchronize()
-    except Exception:  # eager launches if this NCCL build cannot be captured
-        graph = None
         torch.cuda.synchronize()
 
     def run_steps(k):
