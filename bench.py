@@ -1,4 +1,4 @@
-"""Benchmark of the INT4-KV decode hot path (BASELINE config 2 per GPU).
+"""Benchmark of the INT4-KV decode hot path (Llama-3.1-8B decode, B16, S4096, per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -37,7 +37,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "kv-cache-triton_b200"))
 sys.path.insert(0, ROOT)
 
-# workloads: BASELINE config 2 (default) and config 3 (batch-1 long context)
+# workloads: Llama-3.1-8B decode at batch 16 (default), batch-1 long context
 WORKLOADS = {
     "config2": dict(B=16, HQ=32, HKV=8, S=4096),
     "long16k": dict(B=1, HQ=32, HKV=8, S=16384),
@@ -75,24 +75,24 @@ def set_workload(name):
     METRIC = f"INT4-KV decode attention HBM GB/s ({shape}, B{B}, S{S}, G{G})"
 
 
+def workload_config(args, ws):
+    """The ``config`` object, identical for both arms of a run."""
+    model = "llama3.1-70b" if args.workload == "config4" else "llama3.1-8b"
+    return {"workload": f"{args.workload}: {model} single-layer decode step: append 1 token "
+                        "+ INT4 decode attention",
+            "batch": B, "q_heads": HQ, "kv_heads": HKV, "seq_len": S, "d_head": D,
+            "group_size": G,
+            "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
+            "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
+                  f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
+            "bytes_per_step": step_bytes()}
+
+
 def _dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
-
-
-def _traffic():
-    """DRAM bytes per launch of the attention kernel from the committed ncu
-    summary (profiles/kv4_attn_fast_config2.md), or None."""
-    try:
-        with open(os.path.join(ROOT, "profiles", "kv4_attn_fast_config2.md")) as f:
-            for line in f:
-                if line.startswith("| traffic_bytes_per_launch |"):
-                    return int(line.split("|")[2])
-    except Exception:
-        pass
-    return None
 
 
 def _peaks():
@@ -207,29 +207,23 @@ def run_ours(args, ws, rank, local):
         append_op(l)
         attn_op(l)
     torch.cuda.synchronize()
-    g_step, g_pair = [], []
-    for l in range(LAYERS):
-        ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(ga):
-            step_op(l)
-        with torch.cuda.graph(gb):
-            append_op(l)
-            attn_op(l)
-        g_step.append(ga)
-        g_pair.append(gb)
-    # all layers' steps in one graph, as a model's per-token decode graph holds them
+    # The timed region replays a per-token decode graph: one step per layer
+    # for `span` consecutive layers, where span is the largest divisor of
+    # --steps up to LAYERS, so that exactly --steps steps run as whole graph
+    # replays (a model's per-token graph), whatever --steps is.
+    span = max(k for k in range(1, min(LAYERS, args.steps) + 1) if args.steps % k == 0)
     g_all, g_all_pair = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_all):
-        for l in range(LAYERS):
+        for l in range(span):
             step_op(l)
     with torch.cuda.graph(g_all_pair):
-        for l in range(LAYERS):
+        for l in range(span):
             append_op(l)
             attn_op(l)
+    reps = args.steps // span
 
-    for i in range(args.warmup):
-        g_step[i % LAYERS].replay()
-    g_all.replay()
+    for _ in range(max(1, -(-args.warmup // span))):
+        g_all.replay()
     torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
@@ -237,10 +231,8 @@ def run_ours(args, ws, rank, local):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         t0.record(st)
-        for _ in range(args.steps // LAYERS):  # exactly args.steps steps in total
+        for _ in range(reps):
             g_all.replay()
-        for i in range(args.steps % LAYERS):
-            g_step[i].replay()
         t1.record(st)
         torch.cuda.synchronize()
     if ws > 1:
@@ -248,19 +240,20 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
 
-    # the same K steps unfused (append kernel + attention kernel), for comparison
-    for i in range(args.warmup):
-        g_pair[i % LAYERS].replay()
+    # the same steps unfused (append kernel + attention kernel), for comparison
+    for _ in range(max(1, -(-args.warmup // span))):
+        g_all_pair.replay()
     torch.cuda.synchronize()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record(st)
-    for _ in range(args.steps // LAYERS):
+    for _ in range(reps):
         g_all_pair.replay()
-    for i in range(args.steps % LAYERS):
-        g_pair[i].replay()
     p1.record(st)
     torch.cuda.synchronize()
     pair_ms = p0.elapsed_time(p1)
+    gpu_ref = None
+    if not args.no_gpu_reference and ws == 1:
+        gpu_ref = triton_reference_leg(store, q, span, reps, args.warmup, st)
 
     # ---- e2e: public API, pinned host buffers in and out every step ----
     # each step's q, k, v packed in one pinned host row: one copy in per step
@@ -331,13 +324,7 @@ def run_ours(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
         "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
-        "config": {"workload": f"{args.workload}: {"llama3.1-70b" if args.workload == "config4" else "llama3.1-8b"} single-layer decode: append 1 "
-                               "token + INT4 decode attention, one fused launch", "batch": B, "q_heads": HQ, "kv_heads": HKV,
-                   "seq_len": S, "d_head": D, "group_size": G,
-                   "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
-                   "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
-                         f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
-                   "bytes_per_step": step_bytes()},
+        "config": workload_config(args, ws),
         "gpu_launches": args.steps * int(p.kernels),
         "e2e": {"value": round(ws * step_bytes() * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
@@ -347,86 +334,128 @@ def run_ours(args, ws, rank, local):
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "kernel_us": round(attn_avg_ms * 1e3, 2),
                      "unfused_append_plus_attention_us": round(pair_avg_ms * 1e3, 2),
-                     "traffic": _traffic() if args.workload == "config2" else None},
+                     # DRAM bytes come from an ncu capture, not from this run
+                     "traffic": None},
         "clocks": clk.summary(),
         "plan": {"path": int(p.path), "ctas": int(p.ctas), "tiles_per_cta": int(p.tiles_per_cta),
                  "kernels_per_attention": int(p.kernels)},
     }
+    if gpu_ref is not None:
+        line["gpu_reference"] = gpu_ref
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     return line
 
 
-def cpu_baseline(budget_s: float = 15.0, batch_sample: int = 2):
-    batch_sample = min(batch_sample, B)
-    """The reference's CPU formulation on a batch slice of config 2, all host threads."""
+def triton_reference_leg(store, q, span, reps, warmup, st):
+    """Device time of the reference's own fused decode kernel
+    (``kernels/llama3/attention_quant.py:24-286`` of johnchmura/kv-cache-triton,
+    Triton, unmodified, staged in oracle/_ref) on the same caches, q and
+    layer rotation as the timed region above, captured in a CUDA graph the
+    same way.  A baseline leg: it reports, it is not the product."""
+    try:
+        from oracle import triton_ref
+        fn = triton_ref.llama3_attention().attention_forward_quant_gqa
+    except Exception as e:  # Triton missing, or the files were not staged
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    try:
+        def call(l):
+            kp, ks, vp, vs = store.layer(l).views()
+            return fn(q[l], kp, ks, vp, vs, n_q_heads=HQ, n_kv_heads=HKV, group_size=G)
+
+        for l in range(span):
+            call(l)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for l in range(span):
+                call(l)
+        for _ in range(max(1, -(-warmup // span))):
+            graph.replay()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(st)
+        for _ in range(reps):
+            graph.replay()
+        t1.record(st)
+        torch.cuda.synchronize()
+        us = t0.elapsed_time(t1) * 1e3 / (span * reps)
+        import triton
+        return {"kernel": "_attention_fwd_quant_gqa_kernel (reference, Triton "
+                          f"{triton.__version__}, sm_100)",
+                "us_per_step": round(us, 2),
+                "value": round(attn_bytes() / (us * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "note": "attention only (the reference appends with separate quantize + "
+                        "torch.cat launches, not timed here)"}
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def _cpu_ref_problem():
+    """The full workload (all B sequences, S-1 cached tokens + the new one) on
+    host tensors, quantized with the reference's torch path."""
     from oracle import torch_ref
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
     fac = torch.exp(torch.empty(D).uniform_(math.log(0.5), math.log(8.0), generator=g))
-    k = (torch.randn(batch_sample, HKV, S - 1, D, generator=g) * fac).to(torch.bfloat16)
-    v = torch.randn(batch_sample, HKV, S - 1, D, generator=g).to(torch.bfloat16)
+    k = (torch.randn(B, HKV, S - 1, D, generator=g) * fac).to(torch.bfloat16)
+    v = torch.randn(B, HKV, S - 1, D, generator=g).to(torch.bfloat16)
     kp, ks = torch_ref.quantize_int4(k, G)
     vp, vs = torch_ref.quantize_int4(v, G)
     base = {"kp": kp, "ks": ks, "vp": vp, "vs": vs}
-    q = torch.randn(batch_sample, HQ, 1, D, generator=g).to(torch.bfloat16)
-    kn = torch.randn(batch_sample, HKV, 1, D, generator=g).to(torch.bfloat16)
-    vn = torch.randn(batch_sample, HKV, 1, D, generator=g).to(torch.bfloat16)
-    torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)  # warm
+    q = torch.randn(B, HQ, 1, D, generator=g).to(torch.bfloat16)
+    kn = (torch.randn(B, HKV, 1, D, generator=g) * fac).to(torch.bfloat16)
+    vn = torch.randn(B, HKV, 1, D, generator=g).to(torch.bfloat16)
+    return lambda: torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+
+
+_CPU_SAMPLE = ("one decode step of the full workload (B={B}, S={S}) per step through the "
+               "reference's torch CPU route: quantize (half-even) + torch.cat append + "
+               "dequantize to bf16 + repeat_kv + SDPA in bf16; no extrapolation")
+
+
+def cpu_baseline(budget_s: float = 15.0):
+    """The reference's CPU formulation of the same step, all host threads,
+    for about ``budget_s`` seconds (at least 2 steps)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step = _cpu_ref_problem()
+    step()  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+        step()
         n += 1
         el = time.perf_counter() - t0
-        if el > budget_s or n >= 200:
+        if (el > budget_s and n >= 2) or n >= 200:
             break
-    per_sample = el / n
-    frac = batch_sample / B
-    step_s = per_sample / frac
+    step_s = el / n
     return {"value": round(step_bytes() / step_s / 1e9, 3), "unit": "GB/s",
             "us_per_step": round(step_s * 1e6, 1), "cores": threads, "kind": "port",
-            "sample": f"{n} decode steps of batch {batch_sample}/{B} (S={S}) with the reference's "
-                      f"torch CPU path (quantize+cat+dequant+SDPA), scaled x{B // batch_sample}"}
+            "sample": f"{n} steps; " + _CPU_SAMPLE.format(B=B, S=S)}
 
 
 def run_reference(args, ws, rank):
     if rank != 0:
         return None
-    from oracle import torch_ref
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    bs = 1
-    g = torch.Generator().manual_seed(0)
-    fac = torch.exp(torch.empty(D).uniform_(math.log(0.5), math.log(8.0), generator=g))
-    k = (torch.randn(bs, HKV, S - 1, D, generator=g) * fac).to(torch.bfloat16)
-    v = torch.randn(bs, HKV, S - 1, D, generator=g).to(torch.bfloat16)
-    kp, ks = torch_ref.quantize_int4(k, G)
-    vp, vs = torch_ref.quantize_int4(v, G)
-    base = {"kp": kp, "ks": ks, "vp": vp, "vs": vs}
-    q = torch.randn(bs, HQ, 1, D, generator=g).to(torch.bfloat16)
-    kn = torch.randn(bs, HKV, 1, D, generator=g).to(torch.bfloat16)
-    vn = torch.randn(bs, HKV, 1, D, generator=g).to(torch.bfloat16)
+    step = _cpu_ref_problem()
     for _ in range(args.warmup):
-        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        torch_ref.decode_step(dict(base), q, kn, vn, HQ, HKV, G)
+        step()
     el = time.perf_counter() - t0
-    step_s = el / args.steps * (B / bs)  # per full config-2 step
+    step_s = el / args.steps
     value = step_bytes() / step_s / 1e9
-    sample = (f"each step = batch {bs}/{B} of config 2 (S={S}) through the reference's torch "
-              f"CPU path (quantize+cat+dequant+repeat_interleave+SDPA); rate scaled to the "
-              f"full batch")
+    sample = _CPU_SAMPLE.format(B=B, S=S)
     return {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 in, fp32 compute", "data": "synthetic",
+        "ms_per_step": round(step_s * 1e3, 3), "us_per_step": round(step_s * 1e6, 1),
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "llama3.1-8b single-layer decode: append 1 token + INT4 decode "
-                               "attention", "batch": B, "q_heads": HQ, "kv_heads": HKV,
-                   "seq_len": S, "d_head": D, "group_size": G},
+        "config": workload_config(args, ws),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -548,11 +577,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true",
+                    help="skip timing the reference's Triton kernel on the same caches")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--shard", choices=["batch", "seq"], default="batch",
                     help="seq: config-3 sequence sharding over the ranks (strong scaling)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
-                    help="config2 = BASELINE config 2 (the headline); long* = config 3")
+                    help="config2 = 8B decode at batch 16 (the headline); long* = batch-1 long context; "
+                         "config4 = 70B shape, one KV head per GPU")
     args = ap.parse_args()
     set_workload(args.workload)
     args.warmup = max(args.warmup, 3)

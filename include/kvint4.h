@@ -63,8 +63,8 @@ typedef struct kv4_tensor {
 /* Optional knobs for kv4_attention / kv4_attention_partial (pass NULL for defaults). */
 typedef struct kv4_attn_opts {
   int32_t force_generic;   /* 1: use the generic (FFMA, any-stride) kernel */
-  int32_t tiles_per_cta;   /* >0: override the stream-K chunk (tiles of 64 tokens per CTA) */
-  int32_t max_ctas;        /* >0: cap the persistent grid */
+  int32_t tiles_per_cta;   /* >0: override the split-K part length (tiles of 128 tokens per CTA) */
+  int32_t max_ctas;        /* >0: cap the grid (CTAs of the one wave the split-K plan targets) */
   int32_t reserved;
 } kv4_attn_opts;
 
@@ -72,7 +72,7 @@ typedef struct kv4_attn_opts {
 typedef struct kv4_attn_plan {
   int32_t path;            /* 1 = tensor-core TMA kernel, 2 = generic kernel */
   int32_t ctas;            /* CTAs of the main kernel */
-  int32_t tiles_per_cta;   /* stream-K chunk (fast path) */
+  int32_t tiles_per_cta;   /* split-K part length in 128-token tiles (fast path) */
   int32_t units;           /* (batch, kv head, column chunk) work units */
   int32_t max_parts;       /* partial slots per unit */
   int32_t kernels;         /* kernel launches one call makes */
@@ -244,7 +244,9 @@ int kv4_lse_combine(const float *parts_o, const float *parts_lse, int64_t n_part
  * otherwise KV4_ERR_SCRATCH_LIMIT).  Nothing is allocated.  The first call on
  * a device looks up the area's device address (make that first call before
  * any stream capture).  All calls share the area: calls that overlap on the
- * GPU race and must be serialised by the caller.
+ * GPU race and must be serialised by the caller.  `stream` must belong to
+ * the current device (else KV4_ERR_INVALID).  The looked-up address is kept
+ * for the life of the process: do not use the library across a device reset.
  */
 int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_packed,
                           const kv4_tensor *k_scales, const kv4_tensor *v_packed,

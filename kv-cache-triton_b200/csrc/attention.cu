@@ -1191,21 +1191,34 @@ static bool fast_eligible(const kv4_tensor *q, const kv4_tensor *kp, const kv4_t
   return get_encode() != nullptr;
 }
 
+static int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  return dev;
+}
+
+// Occupancy of a fast-path instantiation on the current device.  The dynamic
+// shared-memory attribute is per device (per context), so it is set, and the
+// occupancy queried, once for every device that launches the kernel.
 template <int D, int G, typename ST, bool SPLIT, bool PAGED = false>
 static int occupancy_of() {
-  static int occ = -1;
-  if (occ < 0) {
-    using Cfg = FastCfg<D, G, ST>;
-    cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT, PAGED>, 128,
-                                                      Cfg::SMEM) != cudaSuccess ||
-        o < 1)
-      o = 1;
-    occ = o;
-  }
-  return occ;
+  static std::atomic<int> occ[64];
+  static std::mutex mu;
+  const int dev = current_device();
+  int o = occ[dev].load(std::memory_order_acquire);
+  if (o > 0) return o;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((o = occ[dev].load(std::memory_order_relaxed)) > 0) return o;
+  using Cfg = FastCfg<D, G, ST>;
+  cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+  o = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT, PAGED>, 128,
+                                                    Cfg::SMEM) != cudaSuccess ||
+      o < 1)
+    o = 1;
+  occ[dev].store(o, std::memory_order_release);
+  return o;
 }
 
 static int sm_count() {  // per device, queried once
@@ -1358,12 +1371,18 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
   int smem = Cfg::SMEM;
   if (FP.page > 0) {  // room for the block-table slice after the staged append row
     smem += 16 + FP.bt_slots * 4;
-    static int smem_set = Cfg::SMEM;
-    if (smem > smem_set) {
-      rc = cuda_status(cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      if (rc) return rc;
-      smem_set = smem;
+    // the attribute is per device: remember the largest size set on each
+    static std::atomic<int> smem_set[64];
+    const int dev = current_device();
+    if (smem > std::max(smem_set[dev].load(std::memory_order_acquire), Cfg::SMEM)) {
+      static std::mutex mu;
+      std::lock_guard<std::mutex> lock(mu);
+      if (smem > smem_set[dev].load(std::memory_order_relaxed)) {
+        rc = cuda_status(cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        if (rc) return rc;
+        smem_set[dev].store(smem, std::memory_order_release);
+      }
     }
   }
   kv4_attn_fast<D, G, ST, SPLIT, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
@@ -1824,6 +1843,14 @@ extern "C" int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_pa
   int dev = 0;
   rc = cuda_status(cudaGetDevice(&dev));
   if (rc) return rc;
+  // The scratch address below belongs to the current device; a stream of
+  // another device would make the kernel write to the wrong GPU's array.
+  if (stream != nullptr) {
+    int sdev = -1;
+    rc = cuda_status(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev));
+    if (rc) return rc;
+    if (sdev != dev) return KV4_ERR_INVALID;
+  }
   void *scratch = noalloc_scratch_ptr(dev, &rc);
   if (rc) return rc;
   // The counters (the last `counters` bytes of the area) must start at zero;

@@ -8,6 +8,7 @@ the reference's checks (and raise its ``ValueError`` messages) first.
 from __future__ import annotations
 
 import ctypes
+import functools
 
 import torch
 
@@ -45,12 +46,30 @@ def desc(t: torch.Tensor, host_ok: bool = False) -> Tensor:
     return d
 
 
+def _on_device(fn):
+    """Run ``fn`` with its first tensor's device current.
+
+    The library launches on the current device (tensor maps, occupancy and
+    scratch addresses are per device), so a tensor on cuda:k is handled with
+    cuda:k current even when the caller's current device differs, e.g. a
+    model spread over several GPUs by ``device_map``."""
+    @functools.wraps(fn)
+    def wrapper(t, *args, **kwargs):
+        idx = t.device.index if t.is_cuda else None
+        if idx is None or idx == torch.cuda.current_device():
+            return fn(t, *args, **kwargs)
+        with torch.cuda.device(idx):
+            return fn(t, *args, **kwargs)
+    return wrapper
+
+
 def _stream(dev: torch.device) -> int:
     """Raw handle of the current stream of ``dev`` (no Stream object built)."""
     return torch._C._cuda_getCurrentRawStream(
         dev.index if dev.index is not None else torch.cuda.current_device())
 
 
+@_on_device
 def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, group_size: int,
                   tie: int = _lib.TIE_HALF_AWAY, t_off: int = 0) -> None:
     L = lib()
@@ -59,6 +78,7 @@ def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, g
                                          int(t_off), int(group_size), int(tie), _stream(x.device)))
 
 
+@_on_device
 def append_kv(k, v, k_packed, k_scales, v_packed, v_scales, pos: int, group_size: int,
               tie: int = _lib.TIE_HALF_AWAY) -> None:
     L = lib()
@@ -67,6 +87,7 @@ def append_kv(k, v, k_packed, k_scales, v_packed, v_scales, pos: int, group_size
                                            int(group_size), int(tie), _stream(k.device)))
 
 
+@_on_device
 def dequantize_into(packed: torch.Tensor, scales: torch.Tensor, out: torch.Tensor,
                     group_size: int) -> None:
     L = lib()
@@ -129,6 +150,7 @@ def plan(q, kp, ks, vp, vs, out, group_size, is_causal=False, **kw) -> AttnPlan:
     return p
 
 
+@_on_device
 def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = False,
                    sm_scale: float = 0.0, **kw) -> None:
     L = lib()
@@ -164,6 +186,7 @@ def _with_workspace(dev: torch.device, call, ds, group_size, is_causal, optr) ->
     return rc
 
 
+@_on_device
 def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
                            is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
                            sm_scale: float = 0.0) -> None:
@@ -184,6 +207,7 @@ def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
           _with_workspace(q.device, call, ds, group_size, is_causal, None))
 
 
+@_on_device
 def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
                           is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
                           sm_scale: float = 0.0, **kw) -> None:
@@ -208,6 +232,7 @@ def append_attention_into(q, k_new, v_new, kp, ks, vp, vs, out, group_size: int,
           _with_workspace(q.device, call, ds, group_size, is_causal, optr))
 
 
+@_on_device
 def append_kv_paged(k, v, k_pages, ks_pages, v_pages, vs_pages, slot_mapping: torch.Tensor,
                     group_size: int, tie: int = _lib.TIE_HALF_AWAY) -> None:
     """Quantize k, v [B, Hkv, n, d] into the page pools at ``slot_mapping``
@@ -235,6 +260,7 @@ def paged_plan(q, k_pages, ks_pages, v_pages, vs_pages, max_blocks: int, max_seq
     return p
 
 
+@_on_device
 def attention_paged_into(q, k_pages, ks_pages, v_pages, vs_pages, block_table: torch.Tensor,
                          seq_lens: torch.Tensor, max_seq_len: int, out, group_size: int,
                          is_causal: bool = False, sm_scale: float = 0.0, **kw) -> None:
@@ -261,6 +287,7 @@ def attention_paged_into(q, k_pages, ks_pages, v_pages, vs_pages, block_table: t
                                 ctypes.byref(o) if o else None, _stream(q.device)))
 
 
+@_on_device
 def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, sk_total: int,
                            group_size: int, is_causal: bool = False, sm_scale: float = 0.0,
                            **kw) -> None:
@@ -281,6 +308,7 @@ def attention_partial_into(q, kp, ks, vp, vs, part_o, part_lse, k_offset: int, s
                                   ws.numel() if ws is not None else 0, optr, _stream(q.device)))
 
 
+@_on_device
 def lse_combine_into(parts_o: torch.Tensor, parts_lse: torch.Tensor, out: torch.Tensor) -> None:
     """parts_o f32 [P, rows, d] contiguous, parts_lse f32 [P, rows] contiguous."""
     L = lib()

@@ -60,9 +60,12 @@ def decode_step(cache: dict, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.
     cache["vp"] = torch.cat([cache["vp"], vp], dim=2)
     cache["vs"] = torch.cat([cache["vs"], vs], dim=2)
     d = q.shape[-1]
-    k = dequantize_int4(cache["kp"], cache["ks"], group_size, d)
-    v = dequantize_int4(cache["vp"], cache["vs"], group_size, d)
+    # the reference's CPU route: get_dequantized(out_dtype=q.dtype), then HF
+    # attention (repeat_kv + SDPA) in that dtype (models/llama3/llama3_quant.py:90-99,
+    # kv_cache.py:146-157)
+    k = dequantize_int4(cache["kp"], cache["ks"], group_size, d, out_dtype=q.dtype)
+    v = dequantize_int4(cache["vp"], cache["vs"], group_size, d, out_dtype=q.dtype)
     rep = n_q_heads // n_kv_heads
     k = k.repeat_interleave(rep, dim=1)
     v = v.repeat_interleave(rep, dim=1)
-    return F.scaled_dot_product_attention(q.float(), k, v).to(q.dtype)
+    return F.scaled_dot_product_attention(q, k, v)

@@ -28,14 +28,14 @@ def _cache(b, hkv, s, d, gs, seed):
     return store.layer(0).views()
 
 
-def _noalloc(q, cache, out, gs, causal=False):
+def _noalloc(q, cache, out, gs, causal=False, stream=None):
     """Call the allocation-free entry point straight through the C ABI."""
     from kvint4 import _lib, ops
     L = _lib.lib()
     ds = [ops.desc(t) for t in (q, *cache, out)]
+    st = stream if stream is not None else torch.cuda.current_stream()
     return L.kv4_attention_noalloc(*[ctypes.byref(x) for x in ds], gs, int(causal),
-                                   ctypes.c_float(0.0),
-                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+                                   ctypes.c_float(0.0), ctypes.c_void_p(st.cuda_stream))
 
 
 @pytest.mark.parametrize("order", [0, 1])
@@ -56,7 +56,33 @@ def test_noalloc_matches_workspace_entry_point_two_calls(order):
             out = torch.full_like(q, float("nan"))
             assert _noalloc(q, cache, out, gs) == 0
             torch.cuda.synchronize()
-            np.testing.assert_allclose(f32(out), f32(ref), atol=ATOL[torch.bfloat16], rtol=0)
+            # the same plan and kernel as the workspace entry point: bit-identical
+            assert torch.equal(out, ref)
+
+
+def test_noalloc_causal_multi_query_matches_workspace_entry_point():
+    from kvint4 import ops
+    cache = _cache(2, 4, 2500, 128, 32, 5)
+    q = torch.randn(2, 16, 2, 128, device="cuda", generator=torch.Generator(
+        device="cuda").manual_seed(5)).to(torch.bfloat16)
+    ref = torch.empty_like(q)
+    ops.attention_into(q, *cache, ref, 32, True)
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        assert _noalloc(q, cache, out, 32, causal=True) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_rejects_a_stream_of_another_device():
+    from kvint4 import _lib
+    cache = _cache(2, 2, 3000, 128, 32, 1)
+    q = torch.randn(2, 8, 1, 128, device="cuda:0").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    other = torch.cuda.Stream(device="cuda:1")
+    with torch.cuda.device(0):
+        assert _noalloc(q, cache, out, 32, stream=other) == _lib.KV4_ERR_INVALID
 
 
 def test_noalloc_scratch_covers_default_plans():
