@@ -33,9 +33,16 @@ enum { KV4_F32 = 0, KV4_F16 = 1, KV4_BF16 = 2, KV4_U8 = 3 };
 
 /* rounding of x/scale to the integer code */
 enum {
-  KV4_TIE_HALF_AWAY = 0, /* floor(q+0.5) / ceil(q-0.5): the reference's Triton kernel
-                            (kernels/llama3/quantize.py:62-63) -- default */
-  KV4_TIE_HALF_EVEN = 1  /* torch.round: the reference's CPU path (kernels/llama3/quantize.py:139) */
+  /* default: the reference's Triton GPU kernel (kernels/llama3/quantize.py:47-63):
+     floor(q+0.5) / ceil(q-0.5) rounding, and both fp32 divisions (max/7 and
+     x/scale) as Triton lowers fp32 `/`: PTX div.full.f32 (full-range
+     approximate division), so codes and scales equal Triton's bit for bit */
+  KV4_TIE_HALF_AWAY = 0,
+  /* torch.round with IEEE divisions: the reference's CPU path (kernels/llama3/quantize.py:126-148) */
+  KV4_TIE_HALF_EVEN = 1,
+  /* half-away rounding with IEEE divisions (the Triton formula in exact
+     arithmetic; what the CPU oracle restates bit for bit) */
+  KV4_TIE_HALF_AWAY_IEEE = 2
 };
 
 /* status codes */

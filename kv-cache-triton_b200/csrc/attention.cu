@@ -227,7 +227,7 @@ struct FastParams {
 
 // Quantize one d-wide row with a warp: lane l owns dims [DPL*l, DPL*l + DPL)
 // and returns their packed nibbles (low nibble = even dim) and its group's
-// fp32 scale.  Same arithmetic as quantize_kernel (max |x| / 7, IEEE division).
+// fp32 scale.  Same arithmetic as quantize_kernel for each tie mode.
 template <int D, int G>
 __device__ __forceinline__ void quant_row_warp(const void *x, int dt, int64_t off, int tie,
                                                int lane, uint32_t &w, float &scale) {
@@ -241,13 +241,20 @@ __device__ __forceinline__ void quant_row_warp(const void *x, int dt, int64_t of
   }
 #pragma unroll
   for (int o = 1; o < LPG; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  scale = mx > 0.0f ? __fdiv_rn(mx, 7.0f) : 1.0f;
   w = 0;
+  if (tie == KV4_TIE_HALF_EVEN) {
+    scale = group_scale<KV4_TIE_HALF_EVEN>(mx);
 #pragma unroll
-  for (int e = 0; e < DPL; ++e)
-    w |= (tie == KV4_TIE_HALF_EVEN ? code_of<KV4_TIE_HALF_EVEN>(v[e], scale)
-                                   : code_of<KV4_TIE_HALF_AWAY>(v[e], scale))
-         << (4 * e);
+    for (int e = 0; e < DPL; ++e) w |= code_of<KV4_TIE_HALF_EVEN>(v[e], scale) << (4 * e);
+  } else if (tie == KV4_TIE_HALF_AWAY_IEEE) {
+    scale = group_scale<KV4_TIE_HALF_AWAY_IEEE>(mx);
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) w |= code_of<KV4_TIE_HALF_AWAY_IEEE>(v[e], scale) << (4 * e);
+  } else {
+    scale = group_scale<KV4_TIE_HALF_AWAY>(mx);
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) w |= code_of<KV4_TIE_HALF_AWAY>(v[e], scale) << (4 * e);
+  }
 }
 
 // store the DPL/2 low bytes of w (1, 2 or 4; the address is aligned to that)
@@ -334,6 +341,64 @@ __device__ __forceinline__ uint32_t nib_lo0(uint32_t x) { return lop_nib(x); }
 __device__ __forceinline__ uint32_t nib_hi0(uint32_t x) { return lop_nib(x >> 4); }
 __device__ __forceinline__ uint32_t nib_lo1(uint32_t x) { return lop_nib(x >> 8); }
 __device__ __forceinline__ uint32_t nib_hi1(uint32_t x) { return lop_nib(x >> 12); }
+
+// Nibble extraction into f16x2 values with the f16 magic 1024 (exponent 10:
+// the 10 mantissa bits hold two nibble fields): the low nibble of bytes k and
+// k+2 becomes 1024 + code, the high nibble 1024 + 16 * code, both exact, one
+// LOP3 each, no shift.  The other two bytes need one shift by 8 for both
+// fields: 5 integer ops per 8 codes.
+__device__ __forceinline__ uint32_t h_lo(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(0x000F000Fu), "r"(0x64006400u));
+  return r;  // 1024 + code
+}
+__device__ __forceinline__ uint32_t h_hi(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(0x00F000F0u), "r"(0x64006400u));
+  return r;  // 1024 + 16 * code
+}
+
+// One token row of scales in shared memory, kept as raw words and converted
+// to fp32 where used (one vector load per row instead of one load per group).
+template <int NG, typename ST>
+struct SRow {
+  static constexpr int BYTES = NG * static_cast<int>(sizeof(ST));
+  static constexpr int WORDS = (BYTES + 3) / 4;
+  uint32_t w[WORDS];
+  __device__ __forceinline__ void load(uint32_t a) {
+    if constexpr (BYTES == 2) {
+      w[0] = lds16(a);
+    } else if constexpr (BYTES == 4) {
+      w[0] = lds32(a);
+    } else if constexpr (BYTES == 8) {
+      const uint2 t = lds64(a);
+      w[0] = t.x; w[1] = t.y;
+    } else {
+#pragma unroll
+      for (int k = 0; k < BYTES / 16; ++k) {
+        const uint4 t = lds128(a + 16 * k);
+        w[4 * k] = t.x; w[4 * k + 1] = t.y; w[4 * k + 2] = t.z; w[4 * k + 3] = t.w;
+      }
+    }
+  }
+  __device__ __forceinline__ float get(int gi) const {
+    if constexpr (sizeof(ST) == 4) {
+      return __uint_as_float(w[gi]);
+    } else if constexpr (std::is_same<ST, __nv_bfloat16>::value) {
+      return (gi & 1) ? bf16hi_to_f32(w[gi >> 1]) : bf16lo_to_f32(w[gi >> 1]);
+    } else {
+      return (gi & 1) ? f16hi_to_f32(w[gi >> 1]) : f16lo_to_f32(w[gi >> 1]);
+    }
+  }
+  // (this row's scale of group gi, row b's) as bf16x2, low half = this row
+  __device__ __forceinline__ uint32_t pair_bf16(const SRow &b, int gi) const {
+    if constexpr (std::is_same<ST, __nv_bfloat16>::value) {
+      return prmt(w[gi >> 1], b.w[gi >> 1], (gi & 1) ? 0x7632u : 0x5410u);
+    } else {
+      return pack_bf16x2(get(gi), b.get(gi));
+    }
+  }
+};
 
 template <int NG, typename ST>
 __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
@@ -558,6 +623,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   float o_acc[NCH][2][4];               // O^T fragments [chunk][j][c]
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
+  float col_inv[2];  // score factor of columns 2tg, 2tg+1 (log2 domain)
   int col_lim[2];
   int lim_min = 0;  // smallest key limit over the CTA's columns (warp-uniform)
 
@@ -574,9 +640,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       float gsum[NG];
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) gsum[gi] = 0.0f;
+      float vv[NCH][8];
+      float qmax = 0.0f;
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        float v[8], hi[8], lo[8];
+        float *v = vv[c];
         const int64_t qoff = qbase + (32 * c + 8 * tg) * C.qs[3];
         if (ok && C.q_dtype == KV4_BF16 && C.qs[3] == 1 &&
             (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(C.q) + qoff) & 15) == 0) {
@@ -593,22 +661,64 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
             v[e] = ok ? load_as_f32(C.q, C.q_dtype, qbase + (32 * c + 8 * tg + e) * C.qs[3]) : 0.0f;
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
-          lo[e] = SPLIT ? __bfloat162float(__float2bfloat16_rn(v[e] - hi[e])) : 0.0f;
-          gsum[c / CPG] += hi[e] + lo[e];
-        }
-        // k-step 0: (b0,b1) <- dims (0,4) ; (b2,b3) <- dims (1,5)
-        // k-step 1: (b0,b1) <- dims (2,6) ; (b2,b3) <- dims (3,7)
-        qf[c][0][0] = pack_bf16x2(hi[0], hi[4]);
-        qf[c][0][1] = pack_bf16x2(hi[1], hi[5]);
-        qf[c][1][0] = pack_bf16x2(hi[2], hi[6]);
-        qf[c][1][1] = pack_bf16x2(hi[3], hi[7]);
-        if constexpr (SPLIT) {
+        for (int e = 0; e < 8; ++e) qmax = fmaxf(qmax, fabsf(v[e]));
+      }
+      if constexpr (SPLIT) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          float hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            hi[e] = __bfloat162float(__float2bfloat16_rn(vv[c][e]));
+            lo[e] = __bfloat162float(__float2bfloat16_rn(vv[c][e] - hi[e]));
+            gsum[c / CPG] += -136.0f * (hi[e] + lo[e]);
+          }
+          // k-step 0: (b0,b1) <- dims (0,4) ; (b2,b3) <- dims (1,5)
+          // k-step 1: (b0,b1) <- dims (2,6) ; (b2,b3) <- dims (3,7)
+          qf[c][0][0] = pack_bf16x2(hi[0], hi[4]);
+          qf[c][0][1] = pack_bf16x2(hi[1], hi[5]);
+          qf[c][1][0] = pack_bf16x2(hi[2], hi[6]);
+          qf[c][1][1] = pack_bf16x2(hi[3], hi[7]);
           qfl[c][0][0] = pack_bf16x2(lo[0], lo[4]);
           qfl[c][0][1] = pack_bf16x2(lo[1], lo[5]);
           qfl[c][1][0] = pack_bf16x2(lo[2], lo[6]);
           qfl[c][1][1] = pack_bf16x2(lo[3], lo[7]);
+        }
+        col_inv[0] = col_inv[1] = C.scale_log2;
+      } else {
+        // f16 operands: column g is pre-scaled by sigma = scale_log2 * 2^e,
+        // e chosen so that max |q * sigma| lies in [2^13, 2^14) (exact
+        // power-of-2 range shift, undone by 2^-e on the scores).  Slots that
+        // meet the "1024 + 16 * code" operands take q * sigma / 16.
+        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));
+        const float ml = qmax * C.scale_log2;
+        int e = 0;
+        if (ml > 0.0f) {
+          e = 13 - (static_cast<int>((__float_as_uint(ml) >> 23) & 0xFFu) - 127);
+          e = max(-100, min(100, e));
+        }
+        const float sig = C.scale_log2 * __int_as_float((e + 127) << 23);
+        const float inv = __int_as_float((127 - e) << 23);
+        col_inv[0] = __shfl_sync(0xffffffffu, inv, (2 * tg) * 4);
+        col_inv[1] = __shfl_sync(0xffffffffu, inv, (2 * tg + 1) * 4);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          float w[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = vv[c][k] * sig;
+          qf[c][0][0] = pack_f16x2(w[0], w[4]);
+          qf[c][0][1] = pack_f16x2(w[1] * 0.0625f, w[5] * 0.0625f);
+          qf[c][1][0] = pack_f16x2(w[2], w[6]);
+          qf[c][1][1] = pack_f16x2(w[3] * 0.0625f, w[7] * 0.0625f);
+          // code bias of the rounded operands: a slot of weight w' meets
+          // 1024 + code (x1 slots) or 1024 + 16 * code (x16 slots), whose
+          // (code - 8) value needs -1032 w' resp. -1152 w'
+          const float b1 = f16lo_to_f32(qf[c][0][0]) + f16hi_to_f32(qf[c][0][0]) +
+                           f16lo_to_f32(qf[c][1][0]) + f16hi_to_f32(qf[c][1][0]);
+          const float b16 = f16lo_to_f32(qf[c][0][1]) + f16hi_to_f32(qf[c][0][1]) +
+                            f16lo_to_f32(qf[c][1][1]) + f16hi_to_f32(qf[c][1][1]);
+          gsum[c / CPG] += -1032.0f * b1 - 1152.0f * b16;
         }
       }
       // reduce the per-group sums over the 4 lanes of the quad (tg)
@@ -623,7 +733,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
         const float s0 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg) * 4);
         const float s1 = __shfl_sync(0xffffffffu, gsum[gi], (2 * tg + 1) * 4);
         if (g == 0) {
-          const float b0 = -136.0f * s0, b1 = -136.0f * s1;
+          const float b0 = s0, b1 = s1;
           asm volatile("st.shared.v4.f32 [%0], {%1, %2, %1, %2};" ::"r"(
                            bias_s + ((warp * NG + gi) * 4 + tg) * 16),
                        "f"(b0), "f"(b1)
@@ -868,6 +978,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     // group's K scale in fp32 into s[h][r][cc] (sub-tile h, row g / g+8,
     // column 2tg+cc).
     float s[2][2][2] = {};
+    SRow<NG, ST> krow[2][2];  // K scale rows g, g+8 of both sub-tiles
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) krow[h][r].load(ksb + s_row0 + (16 * h + 8 * r) * Cfg::SROW);
 #pragma unroll
     for (int gi = 0; gi < NG; ++gi) {
       float acc[2][4];
@@ -879,30 +994,40 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const uint32_t x0 = xr[2 * h], x1 = xr[2 * h + 1];
-          const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
-          const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
-          if (cc == 0) {
-            float bq[4];
+          float bq[4];
+          if (cc == 0)
             asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                          : "=f"(bq[0]), "=f"(bq[1]), "=f"(bq[2]), "=f"(bq[3])
                          : "r"(bias_s + ((warp * NG + gi) * 4 + tg) * 16));
-            mma_bf16_16816_c(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bq[0], bq[1],
-                             bq[2], bq[3]);
-          } else
-            mma_bf16_16816(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
-          mma_bf16_16816(acc[h], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
           if constexpr (SPLIT) {
+            const uint32_t a0 = nib_lo0(x0), a1 = nib_lo0(x1), a2 = nib_hi0(x0), a3 = nib_hi0(x1);
+            const uint32_t a4 = nib_lo1(x0), a5 = nib_lo1(x1), a6 = nib_hi1(x0), a7 = nib_hi1(x1);
+            if (cc == 0)
+              mma_bf16_16816_c(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1], bq[0], bq[1],
+                               bq[2], bq[3]);
+            else
+              mma_bf16_16816(acc[h], a0, a1, a2, a3, qf[c][0][0], qf[c][0][1]);
+            mma_bf16_16816(acc[h], a4, a5, a6, a7, qf[c][1][0], qf[c][1][1]);
             mma_bf16_16816(acc[h], a0, a1, a2, a3, qfl[c][0][0], qfl[c][0][1]);
             mma_bf16_16816(acc[h], a4, a5, a6, a7, qfl[c][1][0], qfl[c][1][1]);
+          } else {
+            const uint32_t y0 = x0 >> 8, y1 = x1 >> 8;
+            if (cc == 0)
+              mma_f16_16816_c(acc[h], h_lo(x0), h_lo(x1), h_hi(x0), h_hi(x1), qf[c][0][0],
+                              qf[c][0][1], bq[0], bq[1], bq[2], bq[3]);
+            else
+              mma_f16_16816(acc[h], h_lo(x0), h_lo(x1), h_hi(x0), h_hi(x1), qf[c][0][0],
+                            qf[c][0][1]);
+            mma_f16_16816(acc[h], h_lo(y0), h_lo(y1), h_hi(y0), h_hi(y1), qf[c][1][0],
+                          qf[c][1][1]);
           }
         }
       }
-      constexpr int SS = static_cast<int>(sizeof(ST));
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          const float ks = lds_scale<ST>(ksb + s_row0 + (16 * h + 8 * r) * Cfg::SROW + gi * SS);
+          const float ks = krow[h][r].get(gi);
           s[h][r][0] = fmaf(ks, acc[h][2 * r], s[h][r][0]);
           s[h][r][1] = fmaf(ks, acc[h][2 * r + 1], s[h][r][1]);
         }
@@ -911,8 +1036,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        s[h][r][0] *= C.scale_log2;
-        s[h][r][1] *= C.scale_log2;
+        s[h][r][0] *= col_inv[0];
+        s[h][r][1] *= col_inv[1];
       }
     if (tok0 + WROWS > lim_min) {  // only rows that reach past a key limit need masks
 #pragma unroll
@@ -993,22 +1118,39 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     for (int h = 0; h < 2; ++h) {
       uint32_t pb[NG][2];
       uint32_t pbl[SPLIT ? NG : 1][2];
+      if constexpr (SPLIT) {
 #pragma unroll
-      for (int gi = 0; gi < NG; ++gi) {
-        constexpr int SS = static_cast<int>(sizeof(ST));
-        const float vs0 = lds_scale<ST>(vsb + s_row0 + (16 * h) * Cfg::SROW + gi * SS);
-        const float vs1 = lds_scale<ST>(vsb + s_row0 + (16 * h + 8) * Cfg::SROW + gi * SS);
-        const float a0 = p[h][0][0] * vs0, a1 = p[h][0][1] * vs0;
-        const float c0 = p[h][1][0] * vs1, c1 = p[h][1][1] * vs1;
-        const uint32_t u0 = pack_bf16x2(a0, a1);
-        const uint32_t u1 = pack_bf16x2(c0, c1);
-        pb[gi][0] = movmatrix_trans(u0);
-        pb[gi][1] = movmatrix_trans(u1);
-        if constexpr (SPLIT) {
+        for (int gi = 0; gi < NG; ++gi) {
+          constexpr int SS = static_cast<int>(sizeof(ST));
+          const float vs0 = lds_scale<ST>(vsb + s_row0 + (16 * h) * Cfg::SROW + gi * SS);
+          const float vs1 = lds_scale<ST>(vsb + s_row0 + (16 * h + 8) * Cfg::SROW + gi * SS);
+          const float a0 = p[h][0][0] * vs0, a1 = p[h][0][1] * vs0;
+          const float c0 = p[h][1][0] * vs1, c1 = p[h][1][1] * vs1;
+          const uint32_t u0 = pack_bf16x2(a0, a1);
+          const uint32_t u1 = pack_bf16x2(c0, c1);
+          pb[gi][0] = movmatrix_trans(u0);
+          pb[gi][1] = movmatrix_trans(u1);
           const uint32_t l0 = pack_bf16x2(a0 - bf16lo_to_f32(u0), a1 - bf16hi_to_f32(u0));
           const uint32_t l1 = pack_bf16x2(c0 - bf16lo_to_f32(u1), c1 - bf16hi_to_f32(u1));
           pbl[gi][0] = movmatrix_trans(l0);
           pbl[gi][1] = movmatrix_trans(l1);
+        }
+      } else {
+        // P (bf16) transposed once into the B layout (tokens 2tg, 2tg+1 and
+        // 2tg+8, 2tg+9 of column g), then P' = P * v_scale per group as one
+        // bf16x2 product with the two tokens' scales
+        const uint32_t t0 = movmatrix_trans(pack_bf16x2(p[h][0][0], p[h][0][1]));
+        const uint32_t t1 = movmatrix_trans(pack_bf16x2(p[h][1][0], p[h][1][1]));
+        const uint32_t vrow = vsb + (WROWS * warp + 16 * h + 2 * tg) * Cfg::SROW;
+        SRow<NG, ST> ra, rb, rc, rd;
+        ra.load(vrow);
+        rb.load(vrow + Cfg::SROW);
+        rc.load(vrow + 8 * Cfg::SROW);
+        rd.load(vrow + 9 * Cfg::SROW);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          pb[gi][0] = mul_bf16x2(t0, ra.pair_bf16(rb, gi));
+          pb[gi][1] = mul_bf16x2(t1, rc.pair_bf16(rd, gi));
         }
       }
 #pragma unroll
@@ -1486,7 +1628,7 @@ struct AppendJob {
 
 static int check_append(const AppendJob &A, const Shape &S) {
   if (!A.k || !A.v) return KV4_ERR_INVALID;
-  if (A.tie != KV4_TIE_HALF_AWAY && A.tie != KV4_TIE_HALF_EVEN) return KV4_ERR_INVALID;
+  if (!tie_mode_ok(A.tie)) return KV4_ERR_INVALID;
   if (!is_float(A.k->dtype) || A.v->dtype != A.k->dtype) return KV4_ERR_DTYPE;
   for (int i = 0; i < 4; ++i)
     if (A.k->shape[i] != A.v->shape[i]) return KV4_ERR_SHAPE;

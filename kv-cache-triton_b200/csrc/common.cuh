@@ -233,6 +233,48 @@ __device__ __forceinline__ void mma_bf16_16816_c(float (&d)[4], uint32_t a0, uin
         "f"(c3));
 }
 
+// fp16 operands, fp32 accumulate
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16_16816_c(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                uint32_t a2, uint32_t a3, uint32_t b0,
+                                                uint32_t b1, float c0, float c1, float c2,
+                                                float c3) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %12, %13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2),
+        "f"(c3));
+}
+
+// float -> f16x2 (round to nearest even); `lo` goes to the low 16 bits
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float f16lo_to_f32(uint32_t u) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(u & 0xFFFFu)));
+}
+__device__ __forceinline__ float f16hi_to_f32(uint32_t u) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(u >> 16)));
+}
+
+// bf16x2 product, round to nearest even
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // 8x8 b16 transpose across the warp: lane (g, t) holds row g, cols 2t..2t+1
 // before and after.
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
@@ -241,11 +283,31 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return r;
 }
 
-// INT4 code of x for a group scale: clamp(round(x / scale), -8, 7) + 8 with
-// IEEE division; round = half away from zero or half to even (tie mode).
+// fp32 division as the quantize mode asks: IEEE (div.rn) for the torch path
+// and the exact restatement, PTX div.full.f32 for the reference's Triton
+// kernel (Triton lowers fp32 `/` to that instruction).
+template <int TIE>
+__device__ __forceinline__ float qdiv(float a, float b) {
+  if constexpr (TIE == KV4_TIE_HALF_AWAY) {
+    float r;
+    asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+  } else {
+    return __fdiv_rn(a, b);
+  }
+}
+
+// group scale from max |x|: max / 7 (1.0 for an all-zero group)
+template <int TIE>
+__device__ __forceinline__ float group_scale(float mx) {
+  return mx > 0.0f ? qdiv<TIE>(mx, 7.0f) : 1.0f;
+}
+
+// INT4 code of x for a group scale: clamp(round(x / scale), -8, 7) + 8;
+// round = half away from zero or half to even (tie mode).
 template <int TIE>
 __device__ __forceinline__ uint32_t code_of(float x, float scale) {
-  float q = __fdiv_rn(x, scale);
+  float q = qdiv<TIE>(x, scale);
   float r;
   if (TIE == KV4_TIE_HALF_EVEN) {
     r = rintf(q);
@@ -254,6 +316,10 @@ __device__ __forceinline__ uint32_t code_of(float x, float scale) {
   }
   r = fmaxf(-8.0f, fminf(7.0f, r));
   return static_cast<uint32_t>(static_cast<int>(r) + 8);
+}
+
+static inline bool tie_mode_ok(int t) {
+  return t == KV4_TIE_HALF_AWAY || t == KV4_TIE_HALF_EVEN || t == KV4_TIE_HALF_AWAY_IEEE;
 }
 
 }  // namespace kv4

@@ -2,8 +2,10 @@
 //
 // Arithmetic follows the reference quantizer exactly
 // (kernels/llama3/quantize.py:47-75 Triton kernel, :126-148 torch path):
-//   scale = max|x| / 7 in fp32 (1.0 for an all-zero group), IEEE division
-//   q     = x / scale (IEEE division, un-rounded fp32 scale)
+//   scale = max|x| / 7 in fp32 (1.0 for an all-zero group)
+//   q     = x / scale (un-rounded fp32 scale)
+//   both divisions as the reference path does them: div.full.f32 like the
+//   Triton kernel (default), or IEEE like the torch path
 //   code  = clamp(round(q), -8, 7) + 8, round = half-away (Triton) or
 //           half-even (torch), packed low nibble = even column
 //   the stored scale is the fp32 scale rounded (RN) to the scales dtype.
@@ -101,7 +103,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QParams P) {
     } else {
       for (int e = 0; e < nvalid; ++e) mx = fmaxf(mx, fabsf(to_f32(xg[e * J.xs[3]])));
     }
-    const float scale = mx > 0.0f ? __fdiv_rn(mx, 7.0f) : 1.0f;
+    const float scale = group_scale<TIE>(mx);
 
     // destination row: (i0, i1, i2 + t_off), or the paged slot of (i0, i2)
     int64_t d0 = i0, d2 = i2 + J.t_off;
@@ -198,6 +200,8 @@ static void launch_quant(const QParams &P, int tie, cudaStream_t st) {
   const int grid = grid_for(P.rows * P.ng * P.njobs, threads);
   if (tie == KV4_TIE_HALF_EVEN)
     quantize_kernel<XT, ST, KV4_TIE_HALF_EVEN><<<grid, threads, 0, st>>>(P);
+  else if (tie == KV4_TIE_HALF_AWAY_IEEE)
+    quantize_kernel<XT, ST, KV4_TIE_HALF_AWAY_IEEE><<<grid, threads, 0, st>>>(P);
   else
     quantize_kernel<XT, ST, KV4_TIE_HALF_AWAY><<<grid, threads, 0, st>>>(P);
 }
@@ -227,7 +231,7 @@ static int check_quant_args(const kv4_tensor *x, const kv4_tensor *p, const kv4_
                             int64_t t_off, int G, int tie, int64_t &ng, int64_t &pb) {
   if (!x || !p || !s) return KV4_ERR_INVALID;
   if (G <= 0) return KV4_ERR_INVALID;
-  if (tie != KV4_TIE_HALF_AWAY && tie != KV4_TIE_HALF_EVEN) return KV4_ERR_INVALID;
+  if (!tie_mode_ok(tie)) return KV4_ERR_INVALID;
   if (!is_float_dtype(x->dtype) || !is_float_dtype(s->dtype) || p->dtype != KV4_U8)
     return KV4_ERR_DTYPE;
   const int64_t d = x->shape[3];
@@ -321,7 +325,7 @@ extern "C" int kv4_append_kv_paged(const kv4_tensor *k, const kv4_tensor *v,
       k_pages->shape[1] != k->shape[1] || k_scale_pages->shape[1] != k->shape[1])
     return KV4_ERR_SHAPE;
   if (group_size <= 0) return KV4_ERR_INVALID;
-  if (tie_mode != KV4_TIE_HALF_AWAY && tie_mode != KV4_TIE_HALF_EVEN) return KV4_ERR_INVALID;
+  if (!tie_mode_ok(tie_mode)) return KV4_ERR_INVALID;
   if (!is_float_dtype(k->dtype) || !is_float_dtype(k_scale_pages->dtype) ||
       k_pages->dtype != KV4_U8 || v_pages->dtype != KV4_U8)
     return KV4_ERR_DTYPE;

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 
 from kvint4 import frontend
-from kvint4._lib import TIE_HALF_AWAY, TIE_HALF_EVEN  # noqa: F401
+from kvint4._lib import TIE_HALF_AWAY, TIE_HALF_AWAY_IEEE, TIE_HALF_EVEN  # noqa: F401
 
 
 def _validate_group_size(group_size: int) -> None:

@@ -8,10 +8,12 @@ argument meaning, shapes, dtypes and ``ValueError`` checks
     packed: [..., ceil(d/G)*ceil(G/2)] uint8, low nibble = even column
     scales: [..., ceil(d/G)]         same dtype as x, scale = max|x|/7
 
-Codes are ``clamp(round(x/scale), -8, 7) + 8``.  The default rounding is
-half-away-from-zero, matching the reference's GPU (Triton) kernel
-(:62-63); ``tie_mode=TIE_HALF_EVEN`` reproduces its CPU torch path (:139)
-bit for bit.  All work runs in libkvint4.so on the GPU; CPU tensors raise
+Codes are ``clamp(round(x/scale), -8, 7) + 8``.  The default
+``TIE_HALF_AWAY`` reproduces the reference's GPU (Triton) kernel bit for bit
+(:47-63: half-away rounding, and fp32 divisions as Triton lowers them, PTX
+``div.full.f32``); ``tie_mode=TIE_HALF_EVEN`` reproduces its CPU torch path
+(:126-148, IEEE divisions, ``torch.round``) bit for bit;
+``TIE_HALF_AWAY_IEEE`` is the Triton formula in IEEE arithmetic.  All work runs in libkvint4.so on the GPU; CPU tensors raise
 ``ValueError``.
 """
 
@@ -20,7 +22,7 @@ from __future__ import annotations
 import torch
 
 from kvint4 import frontend
-from kvint4._lib import TIE_HALF_AWAY, TIE_HALF_EVEN  # noqa: F401
+from kvint4._lib import TIE_HALF_AWAY, TIE_HALF_AWAY_IEEE, TIE_HALF_EVEN  # noqa: F401
 
 _SUPPORTED_FLOATS = (torch.bfloat16, torch.float16, torch.float32)
 

@@ -15,7 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkvint4.so")
 
 KV4_F32, KV4_F16, KV4_BF16, KV4_U8 = 0, 1, 2, 3
-TIE_HALF_AWAY, TIE_HALF_EVEN = 0, 1
+TIE_HALF_AWAY, TIE_HALF_EVEN, TIE_HALF_AWAY_IEEE = 0, 1, 2
 KV4_OK = 0
 KV4_ERR_INVALID, KV4_ERR_DTYPE, KV4_ERR_SHAPE, KV4_ERR_LAYOUT = 1, 2, 3, 4
 KV4_ERR_WORKSPACE, KV4_ERR_CUDA, KV4_ERR_UNSUPPORTED, KV4_ERR_DEVICE = 5, 6, 7, 8

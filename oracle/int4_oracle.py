@@ -30,7 +30,12 @@ import math
 
 import numpy as np
 
-TIE_HALF_AWAY = 0  # Triton GPU kernel, kernels/llama3/quantize.py:62-63
+# Half-away rounding of the Triton kernel's formula (kernels/llama3/quantize.py:47-63)
+# in IEEE arithmetic: the library's KV4_TIE_HALF_AWAY_IEEE bit for bit.  The
+# library's default KV4_TIE_HALF_AWAY also takes Triton's fp32 divisions (PTX
+# div.full.f32), whose last bit this restatement does not model; that mode is
+# pinned against the reference's own Triton kernel on the GPU instead.
+TIE_HALF_AWAY = 0
 TIE_HALF_EVEN = 1  # torch CPU path (torch.round), kernels/llama3/quantize.py:139
 
 

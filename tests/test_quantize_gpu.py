@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from golden_io import cases, load, to_f32
-from helpers import DT_NAME, TORCH_DT, f32, oracle_quant
+from helpers import DT_NAME, TORCH_DT, assert_codes_near_oracle, f32, oracle_quant
 from oracle import int4_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -54,33 +54,59 @@ def test_quantize_half_even_matches_golden_bit_exact(case):
 
 
 @pytest.mark.parametrize("case", cases(Q))
-def test_quantize_half_away_matches_oracle_bit_exact(case):
-    """Default (Triton-compatible) rounding vs the oracle's restatement."""
-    from kernels.llama3.quantize import quantize_int4
+def test_quantize_half_away_ieee_matches_oracle_bit_exact(case):
+    """Half-away rounding with IEEE divisions vs the oracle's restatement."""
+    from kernels.llama3.quantize import TIE_HALF_AWAY_IEEE, quantize_int4
     x = _x_from_golden(case)
     gs = int(Q[case + ".group_size"])
-    packed, scales = quantize_int4(x, group_size=gs)
+    packed, scales = quantize_int4(x, group_size=gs, tie_mode=TIE_HALF_AWAY_IEEE)
     p_ref, s_ref = oracle_quant(x, gs, orc.TIE_HALF_AWAY, x.dtype)
     np.testing.assert_array_equal(packed.cpu().numpy(), p_ref)
     np.testing.assert_array_equal(f32(scales), s_ref)
 
 
+@pytest.mark.parametrize("case", cases(Q))
+def test_quantize_default_mode_near_oracle(case):
+    """The default mode (the reference Triton kernel's arithmetic) differs
+    from the IEEE restatement only at rounding boundaries."""
+    from kernels.llama3.quantize import quantize_int4
+    x = _x_from_golden(case)
+    if x.numel() == 0:
+        pytest.skip("empty")
+    gs = int(Q[case + ".group_size"])
+    packed, scales = quantize_int4(x, group_size=gs)
+    assert_codes_near_oracle(x, gs, packed, scales)
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
 @pytest.mark.parametrize("gs", [32, 64, 128])
-@pytest.mark.parametrize("tie", [0, 1])
+@pytest.mark.parametrize("tie", [2, 1])
 def test_quantize_large_random_bit_exact(dtype, gs, tie):
     from kernels.llama3.quantize import quantize_int4
     g = torch.Generator().manual_seed(gs + tie)
     x = (torch.randn(4, 8, 257, 128, generator=g) * 3).to(TORCH_DT[dtype])
     x[0, 0, 0, :] = 0  # an all-zero row -> scale 1
     packed, scales = quantize_int4(x.cuda(), group_size=gs, tie_mode=tie)
-    p_ref, s_ref = oracle_quant(x, gs, tie, x.dtype)
+    p_ref, s_ref = oracle_quant(x, gs, orc.TIE_HALF_AWAY if tie == 2 else tie, x.dtype)
     np.testing.assert_array_equal(packed.cpu().numpy(), p_ref)
     np.testing.assert_array_equal(f32(scales), s_ref)
 
 
-def test_quantize_strided_input_and_odd_shapes():
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+def test_quantize_default_mode_large_random_near_oracle(dtype):
     from kernels.llama3.quantize import quantize_int4
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(8, 4, 257, 128, generator=g) * 3).to(TORCH_DT[dtype])
+    packed, scales = quantize_int4(x.cuda(), group_size=32)
+    assert_codes_near_oracle(x, 32, packed, scales)
+
+
+def test_quantize_strided_input_and_odd_shapes():
+    from functools import partial
+
+    from kernels.llama3.quantize import TIE_HALF_AWAY_IEEE
+    from kernels.llama3.quantize import quantize_int4 as q4
+    quantize_int4 = partial(q4, tie_mode=TIE_HALF_AWAY_IEEE)
     g = torch.Generator().manual_seed(5)
     base = torch.randn(3, 40, 6, 128, generator=g).to(torch.bfloat16).cuda()
     x = base.transpose(1, 2)  # [3, 6, 40, 128] non-contiguous, like k_proj(...).transpose(1, 2)
