@@ -1136,21 +1136,16 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
           pbl[gi][1] = movmatrix_trans(l1);
         }
       } else {
-        // P (bf16) transposed once into the B layout (tokens 2tg, 2tg+1 and
-        // 2tg+8, 2tg+9 of column g), then P' = P * v_scale per group as one
-        // bf16x2 product with the two tokens' scales
-        const uint32_t t0 = movmatrix_trans(pack_bf16x2(p[h][0][0], p[h][0][1]));
-        const uint32_t t1 = movmatrix_trans(pack_bf16x2(p[h][1][0], p[h][1][1]));
-        const uint32_t vrow = vsb + (WROWS * warp + 16 * h + 2 * tg) * Cfg::SROW;
-        SRow<NG, ST> ra, rb, rc, rd;
-        ra.load(vrow);
-        rb.load(vrow + Cfg::SROW);
-        rc.load(vrow + 8 * Cfg::SROW);
-        rd.load(vrow + 9 * Cfg::SROW);
+        // P' = P * v_scale in fp32 (one rounding to bf16), the scale rows of
+        // tokens g and g+8 loaded once each, then transposed into the B layout
+        SRow<NG, ST> ra, rc;
+        ra.load(vsb + s_row0 + (16 * h) * Cfg::SROW);
+        rc.load(vsb + s_row0 + (16 * h + 8) * Cfg::SROW);
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
-          pb[gi][0] = mul_bf16x2(t0, ra.pair_bf16(rb, gi));
-          pb[gi][1] = mul_bf16x2(t1, rc.pair_bf16(rd, gi));
+          const float vs0 = ra.get(gi), vs1 = rc.get(gi);
+          pb[gi][0] = movmatrix_trans(pack_bf16x2(p[h][0][0] * vs0, p[h][0][1] * vs0));
+          pb[gi][1] = movmatrix_trans(pack_bf16x2(p[h][1][0] * vs1, p[h][1][1] * vs1));
         }
       }
 #pragma unroll

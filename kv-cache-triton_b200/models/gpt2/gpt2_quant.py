@@ -2,23 +2,44 @@
 
 Drop-in for the reference's ``models/gpt2/gpt2_quant.py``
 (``GPT2AttentionQuantized`` :16-138, ``replace_gpt2_attention_with_quantized``
-:141-157), with its routing (:93-118): the fused kernel runs for
-self-attention on CUDA when the query is a single token or no mask is given
-(and not in eager "reorder_and_upcast" mode); otherwise the cache is
-dequantized on the GPU and the stock attention function runs.
+:141-157).  The module owns one decision only, where the cached attention
+runs; everything else is Hugging Face's ``GPT2Attention``:
+
+* self-attention with a ``QuantizedKVCache`` on CUDA, fp16/fp32 activations,
+  a one-token query or no mask, and not the eager "reorder and upcast" mode
+  (the reference's condition, :93-99): the projections run here, K/V are
+  quantized into the cache and the fused INT4 kernel attends over the packed
+  cache (a one-token step is one launch: append and attention fused);
+* any other call with a ``QuantizedKVCache`` runs HF's forward against a thin
+  cache view that quantizes the new K/V into the INT4 cache and hands HF the
+  dequantized cache (the reference's fallback, :109-126);
+* without a ``QuantizedKVCache`` (or for cross-attention) HF's forward runs
+  unchanged.
 """
 
 from __future__ import annotations
 
-from typing import Callable, Optional
+import types
 
 import torch
-from transformers.cache_utils import EncoderDecoderCache
-from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
-from transformers.models.gpt2.modeling_gpt2 import GPT2Attention, eager_attention_forward
+from transformers.models.gpt2.modeling_gpt2 import GPT2Attention
 
 from kernels.gpt2.attention_quant import attention_forward_quant
 from models.gpt2.kv_cache import QuantizedKVCache
+
+
+class _DequantizedCacheView:
+    """What HF's forward sees of a ``QuantizedKVCache`` on the fallback route:
+    ``update`` quantizes the new K/V into the INT4 cache and returns the whole
+    layer dequantized in the activations' dtype."""
+
+    def __init__(self, cache: QuantizedKVCache):
+        self.cache = cache
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        self.cache.update(key_states, value_states, layer_idx, cache_kwargs)
+        k, v = self.cache.get_dequantized(layer_idx)
+        return k.to(key_states.dtype), v.to(value_states.dtype)
 
 
 class GPT2AttentionQuantized(GPT2Attention):
@@ -29,125 +50,51 @@ class GPT2AttentionQuantized(GPT2Attention):
         super().__init__(config, is_cross_attention=is_cross_attention, layer_idx=layer_idx)
         self.quant_group_size = int(group_size)
 
-    def forward(
-        self,
-        hidden_states,
-        past_key_values=None,
-        cache_position: Optional[torch.LongTensor] = None,
-        attention_mask: Optional[torch.FloatTensor] = None,
-        head_mask: Optional[torch.FloatTensor] = None,
-        encoder_hidden_states: Optional[torch.Tensor] = None,
-        encoder_attention_mask: Optional[torch.FloatTensor] = None,
-        output_attentions: Optional[bool] = False,
-        **kwargs,
-    ):
-        is_cross_attention = encoder_hidden_states is not None
-        quant_cache = past_key_values if isinstance(past_key_values, QuantizedKVCache) else None
-        is_updated = False
-        curr_past_key_value = None
-        if past_key_values is not None and quant_cache is None:
-            if isinstance(past_key_values, EncoderDecoderCache):
-                is_updated = past_key_values.is_updated.get(self.layer_idx)
-                curr_past_key_value = (past_key_values.cross_attention_cache if is_cross_attention
-                                       else past_key_values.self_attention_cache)
-            else:
-                curr_past_key_value = past_key_values
+    def _fused_ok(self, hidden_states: torch.Tensor, attention_mask) -> bool:
+        if not hidden_states.is_cuda or hidden_states.dtype not in (torch.float16, torch.float32):
+            return False
+        if self.config._attn_implementation == "eager" and self.reorder_and_upcast_attn:
+            return False
+        return hidden_states.shape[-2] == 1 or attention_mask is None
 
-        if is_cross_attention:
-            if not hasattr(self, "q_attn"):
-                raise ValueError(
-                    "If class is used as cross attention, the weights `q_attn` have to be defined. "
-                    "Please make sure to instantiate class with `GPT2Attention(..., is_cross_attention=True)`.")
-            query_states = self.q_attn(hidden_states)
-            attention_mask = encoder_attention_mask
-            if past_key_values is not None and quant_cache is None and is_updated:
-                key_states = curr_past_key_value.layers[self.layer_idx].keys
-                value_states = curr_past_key_value.layers[self.layer_idx].values
-            else:
-                key_states, value_states = self.c_attn(encoder_hidden_states).split(
-                    self.split_size, dim=2)
-                shape_kv = (*key_states.shape[:-1], -1, self.head_dim)
-                key_states = key_states.view(shape_kv).transpose(1, 2)
-                value_states = value_states.view(shape_kv).transpose(1, 2)
+    def forward(self, hidden_states, past_key_values=None, attention_mask=None, **kwargs):
+        cache = past_key_values if isinstance(past_key_values, QuantizedKVCache) else None
+        if cache is None or kwargs.get("encoder_hidden_states") is not None:
+            return super().forward(hidden_states, past_key_values=past_key_values,
+                                   attention_mask=attention_mask, **kwargs)
+        if not self._fused_ok(hidden_states, attention_mask):
+            return super().forward(hidden_states, past_key_values=_DequantizedCacheView(cache),
+                                   attention_mask=attention_mask, **kwargs)
+
+        # [B, s, 3 * hidden] -> three [B, heads, s, head_dim] views
+        q, k, v = (t.unflatten(-1, (-1, self.head_dim)).transpose(1, 2)
+                   for t in self.c_attn(hidden_states).split(self.split_size, dim=2))
+        b, heads, s, d = q.shape
+        # the kernel writes [B, s, heads, d] directly: c_proj's input needs no copy
+        out = torch.empty(b, s, heads, d, dtype=q.dtype, device=q.device)
+        causal = attention_mask is None and s > 1
+        if s == 1 and k.shape[-2] == 1:
+            cache.append_attend(q, k, v, self.layer_idx, out.transpose(1, 2), n_q_heads=heads,
+                                n_kv_heads=heads, is_causal=causal)
         else:
-            query_states, key_states, value_states = self.c_attn(hidden_states).split(
-                self.split_size, dim=2)
-            shape_kv = (*key_states.shape[:-1], -1, self.head_dim)
-            key_states = key_states.view(shape_kv).transpose(1, 2)
-            value_states = value_states.view(shape_kv).transpose(1, 2)
+            cache.append(k, v, self.layer_idx)
+            attention_forward_quant(q, *cache.get_quantized(self.layer_idx),
+                                    group_size=self.quant_group_size, is_causal=causal,
+                                    out=out.transpose(1, 2))
+        y = self.resid_dropout(self.c_proj(out.flatten(-2)))
+        return y, None
 
-        shape_q = (*query_states.shape[:-1], -1, self.head_dim)
-        query_states = query_states.view(shape_q).transpose(1, 2)
 
-        # one-token decode on the fused kernel: the append happens inside the
-        # attention launch (QuantizedKVCache.append_attend) below
-        fuse_append = (
-            quant_cache is not None
-            and not is_cross_attention
-            and query_states.is_cuda
-            and query_states.shape[-2] == 1
-            and key_states.shape[-2] == 1
-            and not (self.config._attn_implementation == "eager" and self.reorder_and_upcast_attn)
-            and query_states.dtype in (torch.float16, torch.float32)
-        )
-        if quant_cache is not None and not is_cross_attention:
-            if not fuse_append:
-                quant_cache.append(key_states, value_states, self.layer_idx)
-        elif (past_key_values is not None and not is_cross_attention) or (
-                past_key_values is not None and is_cross_attention and not is_updated):
-            key_states, value_states = curr_past_key_value.update(key_states, value_states,
-                                                                  self.layer_idx)
-            if is_cross_attention:
-                past_key_values.is_updated[self.layer_idx] = True
-
-        is_causal = attention_mask is None and query_states.shape[-2] > 1 and not is_cross_attention
-        using_eager = self.config._attn_implementation == "eager"
-        attention_interface: Callable = eager_attention_forward
-        if not using_eager:
-            attention_interface = ALL_ATTENTION_FUNCTIONS[self.config._attn_implementation]
-
-        use_quant_kernel = (
-            quant_cache is not None
-            and not is_cross_attention
-            and query_states.is_cuda
-            and not (using_eager and self.reorder_and_upcast_attn)
-            and (query_states.shape[-2] == 1 or attention_mask is None)
-            and query_states.dtype in (torch.float16, torch.float32)
-        )
-
-        if using_eager and self.reorder_and_upcast_attn:
-            if quant_cache is not None and not is_cross_attention:
-                key_states, value_states = quant_cache.get_dequantized(self.layer_idx)
-            attn_output, attn_weights = self._upcast_and_reordered_attn(
-                query_states, key_states, value_states, attention_mask, head_mask)
-        elif use_quant_kernel:
-            b, h, sq, d = query_states.shape
-            out = torch.empty(b, sq, h, d, dtype=query_states.dtype, device=query_states.device)
-            if fuse_append:
-                quant_cache.append_attend(query_states, key_states, value_states, self.layer_idx,
-                                          out.transpose(1, 2), n_q_heads=h, n_kv_heads=h,
-                                          is_causal=is_causal)
-            else:
-                k_packed, k_scales, v_packed, v_scales = quant_cache.get_quantized(self.layer_idx)
-                attention_forward_quant(query_states, k_packed, k_scales, v_packed, v_scales,
-                                        group_size=self.quant_group_size, is_causal=is_causal,
-                                        out=out.transpose(1, 2))
-            attn_output = out
-            attn_weights = None
-        else:
-            if quant_cache is not None and not is_cross_attention:
-                key_states, value_states = quant_cache.get_dequantized(self.layer_idx)
-                key_states = key_states.to(query_states.dtype)
-                value_states = value_states.to(query_states.dtype)
-            attn_output, attn_weights = attention_interface(
-                self, query_states, key_states, value_states, attention_mask, head_mask=head_mask,
-                dropout=self.attn_dropout.p if self.training else 0.0, is_causal=is_causal,
-                **kwargs)
-
-        attn_output = attn_output.reshape(*attn_output.shape[:-2], -1).contiguous()
-        attn_output = self.c_proj(attn_output)
-        attn_output = self.resid_dropout(attn_output)
-        return attn_output, attn_weights
+def _retarget(module: torch.nn.Module, cls: type, **attrs) -> None:
+    """Turn ``module`` into an instance of its subclass ``cls`` in place: its
+    parameters, buffers, device placement and any ``accelerate`` dispatch
+    hook stay where they are; a hook's saved forward is re-bound so that it
+    calls the subclass's forward."""
+    module.__class__ = cls
+    for name, value in attrs.items():
+        setattr(module, name, value)
+    if hasattr(module, "_old_forward"):  # accelerate's add_hook_to_module
+        module._old_forward = types.MethodType(cls.forward, module)
 
 
 def replace_gpt2_attention_with_quantized(model: torch.nn.Module, group_size: int = 32) -> None:
@@ -156,14 +103,7 @@ def replace_gpt2_attention_with_quantized(model: torch.nn.Module, group_size: in
     if blocks is None:
         raise ValueError("expected a GPT2 model with .transformer.h blocks")
     for block in blocks:
-        old = block.attn
-        if isinstance(old, GPT2AttentionQuantized):
-            old.quant_group_size = int(group_size)
-            continue
-        device = next(old.parameters()).device
-        ref_dtype = next(old.parameters()).dtype
-        new = GPT2AttentionQuantized(old.config, layer_idx=old.layer_idx, group_size=group_size)
-        new.load_state_dict(old.state_dict())
-        new.to(device=device, dtype=ref_dtype)
-        new.train(old.training)
-        block.attn = new
+        attn = block.attn
+        if type(attn) is not GPT2AttentionQuantized and not isinstance(attn, GPT2Attention):
+            raise ValueError(f"unexpected attention module {type(attn).__name__}")
+        _retarget(attn, GPT2AttentionQuantized, quant_group_size=int(group_size))

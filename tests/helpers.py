@@ -20,7 +20,7 @@ def f32(t: torch.Tensor) -> np.ndarray:
 
 def kv_inputs(b, hkv, s, d, dtype=torch.bfloat16, seed=0, outliers=True, device="cpu"):
     """K, V ~ N(0,1) with every K channel scaled by a factor log-uniform in
-    [0.5, 8] (BASELINE config 2's outlier channels)."""
+    [0.5, 8] (the outlier channels of the Llama-3.1-8B benchmark inputs)."""
     g = torch.Generator().manual_seed(seed)
     k = torch.randn(b, hkv, s, d, generator=g)
     if outliers:

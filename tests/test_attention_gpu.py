@@ -129,9 +129,17 @@ def test_cache_views_read_in_place_and_odd_lengths():
     np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
 
 
-def test_config2_shape_full_size_properties():
-    """BASELINE config 2 shape (B16, 32/8 heads, S 4096, d 128, G 32): output
-    against the oracle on a batch slice, split invariance, determinism."""
+def _oracle_rows(q, kp, ks, vp, vs, hq, hkv):
+    """The float64 oracle one batch row at a time (full-size shapes)."""
+    return np.concatenate([
+        oracle_attention(q[b:b + 1], kp[b:b + 1], ks[b:b + 1], vp[b:b + 1], vs[b:b + 1],
+                         n_q_heads=hq, n_kv_heads=hkv, group_size=32)
+        for b in range(q.shape[0])])
+
+
+def test_llama8b_batch16_every_row_matches_oracle():
+    """Llama-3.1-8B decode shape (B16, 32/8 heads, S 4096, d 128, G 32): every
+    batch row against the oracle; split invariance; determinism."""
     from kernels.llama3.attention_quant import attention_forward_quant_gqa
     from kernels.llama3.quantize import quantize_int4
     from kvint4 import frontend
@@ -145,10 +153,70 @@ def test_config2_shape_full_size_properties():
     one = frontend.attention(q, kp, ks, vp, vs, n_q_heads=32, n_kv_heads=8, group_size=32,
                              is_causal=False, tiles_per_cta=64)  # one CTA per unit
     assert (out.float() - one.float()).abs().max().item() <= 2e-2
-    sl = slice(0, 2)
-    ref = oracle_attention(q[sl], kp[sl], ks[sl], vp[sl], vs[sl], n_q_heads=32, n_kv_heads=8,
-                           group_size=32)
-    np.testing.assert_allclose(f32(out[sl]), ref, atol=2e-2, rtol=0)
+    ref = _oracle_rows(q, kp, ks, vp, vs, 32, 8)
+    np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
+
+
+def test_llama70b_head_shard_shape_every_row_matches_oracle():
+    """Llama-3.1-70B decode with one KV head per GPU: B32, 8 q heads over 1 KV
+    head (GQA 8), S 16384, d 128, G 32; every batch row against the oracle."""
+    from kernels.llama3.attention_quant import attention_forward_quant_gqa
+    from kernels.llama3.quantize import quantize_int4
+    k, v = kv_inputs(32, 1, 16384, 128, device="cuda", seed=70)
+    q = torch.randn(32, 8, 1, 128, device="cuda").to(torch.bfloat16)
+    kp, ks = quantize_int4(k, 32)
+    vp, vs = quantize_int4(v, 32)
+    out = attention_forward_quant_gqa(q, kp, ks, vp, vs, n_q_heads=8, n_kv_heads=1)
+    assert _plan_path(q, (kp, ks, vp, vs), 32) == 1
+    ref = _oracle_rows(q, kp, ks, vp, vs, 8, 1)
+    np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
+
+
+def test_gpt2_small_decode_entry_point_matches_oracle():
+    """GPT-2-small decode through kernels.gpt2.attention_quant.attention_forward_quant:
+    fp32 q [4, 12, 1, 64], K/V [4, 12, 1024, 64] N(0,1), G 32, fp16 scales
+    (reference tests/gpt2/test_attention_quant.py:13-62)."""
+    from kernels.gpt2.attention_quant import attention_forward_quant
+    from kernels.gpt2.quantize import quantize_int4
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(4, 12, 1, 64, generator=g).cuda()
+    k = torch.randn(4, 12, 1024, 64, generator=g).cuda()
+    v = torch.randn(4, 12, 1024, 64, generator=g).cuda()
+    kp, ks = quantize_int4(k, group_size=32)
+    vp, vs = quantize_int4(v, group_size=32)
+    assert ks.dtype == torch.float16
+    out = attention_forward_quant(q, kp, ks, vp, vs, group_size=32)
+    assert out.dtype == torch.float32 and out.shape == q.shape
+    ref = oracle_attention(q, kp, ks, vp, vs, n_q_heads=12, n_kv_heads=12, group_size=32)
+    np.testing.assert_allclose(f32(out), ref, atol=1e-3, rtol=0)
+    # fp16 q as well (the reference accepts fp16 and fp32)
+    out16 = attention_forward_quant(q.half(), kp, ks, vp, vs, group_size=32)
+    ref16 = oracle_attention(q.half(), kp, ks, vp, vs, n_q_heads=12, n_kv_heads=12,
+                             group_size=32)
+    np.testing.assert_allclose(f32(out16), ref16, atol=5e-3, rtol=0)
+
+
+def test_gpt2_golden_mha_case():
+    """The golden d64 MHA decode case through the GPT-2 entry point."""
+    from kernels.gpt2.attention_quant import attention_forward_quant
+    names = [c for c in cases(A) if "mha" in c and "d64" in c]
+    if not names:
+        pytest.skip("no golden MHA d64 case")
+    for case in names:
+        b, hq, hkv, sq, sk, d, gs, causal = (int(x) for x in A[case + ".meta"])
+        qdt = str(A[case + ".q_dtype"])
+        sdt = str(A[case + ".scale_dtype"])
+        if qdt not in ("f16", "f32") or sdt != "f16" or hq != hkv:
+            continue
+        tdt = {"f16": torch.float16, "f32": torch.float32}
+        q = torch.from_numpy(to_f32(A[case + ".q"], qdt)).to(tdt[qdt]).cuda()
+        ks = torch.from_numpy(to_f32(A[case + ".k_scales"], sdt)).half().cuda()
+        vs = torch.from_numpy(to_f32(A[case + ".v_scales"], sdt)).half().cuda()
+        kp = torch.from_numpy(A[case + ".k_packed"]).cuda()
+        vp = torch.from_numpy(A[case + ".v_packed"]).cuda()
+        out = attention_forward_quant(q, kp, ks, vp, vs, group_size=gs, is_causal=bool(causal))
+        np.testing.assert_allclose(f32(out), A[case + ".out_ref_f32"], atol=ATOL[tdt[qdt]],
+                                   rtol=0)
 
 
 A = load("attn_cases.npz")
@@ -208,7 +276,7 @@ def test_no_device_error_flag_after_runs():
 
 @pytest.mark.parametrize("sk", [16384, 131072])
 def test_config3_long_context_batch1(sk):
-    """BASELINE config 3 shape (B=1, 32/8 heads, d=128, G=32) at full length:
+    """Batch-1 long-context shape (B=1, 32/8 heads, d=128, G=32) at full length:
     KV head 0 (q heads 0-3) against the oracle, plus agreement of the fused
     kernel with a 4-way sequence-shard decomposition for all heads."""
     from kvint4 import ops
