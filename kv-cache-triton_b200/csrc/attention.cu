@@ -188,6 +188,7 @@ constexpr int TOK = 128;   // tokens per pipeline stage (4 warps x 32 rows)
 constexpr int NWARP = 4;
 constexpr int WROWS = 32;  // token rows per warp per stage (two m16 sub-tiles)
 constexpr int NCOL = 8;    // (head, query row) columns per CTA = MMA N
+constexpr int MERGE_GROUP = 8;  // split-K parts merged per first-level group
 
 struct FastParams {
   AttnCommon c;
@@ -199,7 +200,9 @@ struct FastParams {
   int maxp;       // partial slots per unit
   float *ws_o;    // [units*maxp][NCOL][d]
   float *ws_lse;  // [units*maxp][NCOL]   (log2 domain)
-  int *counters;  // [units] finished-segment counts (zero between calls)
+  int *counters;  // [units] finished-segment counts (zero between calls); the
+                  // [units][ngroups] first-level counters sit right before
+  int units;
   const char *ks, *vs;         // scale tensors
   int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
   // Fused quantize-on-append (app_row >= 0): the new token's K/V rows
@@ -318,7 +321,16 @@ struct FastCfg {
   static constexpr int STAGE = ((2 * KP + 2 * KS) + 1023) / 1024 * 1024;
   // 3 x 18 KB at d=128 with 3 CTAs/SM (measured faster than 2 stages at 4
   // CTAs/SM: 64K context 37.4 -> 33.6 us); d=256 keeps 2 stages so 2 CTAs fit
-  static constexpr int STAGES = (D == 256) ? 2 : 3;
+#ifndef KV4_RELEASE_ATOM
+#define KV4_RELEASE_ATOM "atom.acq_rel.cta.shared::cta.add.u32"
+#endif
+#ifndef KV4_STAGES
+#define KV4_STAGES 3
+#endif
+#ifndef KV4_MINB
+#define KV4_MINB 3
+#endif
+  static constexpr int STAGES = (D == 256) ? 2 : KV4_STAGES;
   static constexpr int MERGE = NWARP * NCOL * D * 4;
   static_assert(MERGE <= STAGES * STAGE, "merge buffer aliases the stages");
   static constexpr int APP = 2 * P + 2 * SROW;  // staged new row (fused append)
@@ -442,7 +454,7 @@ __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
 }
 
 template <int D, int G, typename ST, bool SPLIT, bool PAGED>
-__global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
+__global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
                   const __grid_constant__ CUtensorMap tm_vp) {
   using Cfg = FastCfg<D, G, ST>;
@@ -489,6 +501,25 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   }
   const int ntiles = max(0, min(t_end, (sk_u + TOK - 1) / TOK) - t_begin);
   if (ntiles <= 0 && !paged) return;
+
+  // q of this lane's B-operand column (n = g), requested before anything
+  // else so that it is not queued behind the CTA's tile loads in HBM
+  const int q_n = u_hc * NCOL + g;
+  const bool q_ok = q_n < P.ncols;
+  const int64_t q_base = q_ok ? u_b * C.qs[0] + (u_kvh * C.R + q_n % C.R) * C.qs[1] +
+                                    (q_n / C.R) * C.qs[2]
+                              : 0;
+  const bool q_vec =
+      q_ok && C.q_dtype == KV4_BF16 && C.qs[3] == 1 &&
+      (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(C.q) + q_base + 8 * tg) &
+       15) == 0;
+  uint4 q_raw[NCH];
+  if (q_vec) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      q_raw[c] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(C.q) +
+                                                       q_base + 32 * c + 8 * tg));
+  }
 
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
@@ -630,13 +661,10 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
   auto load_unit = [&]() {
     const int hcid = u_hc, b = u_b, kvh = u_kvh;
     {
-      // B operand column n = g
-      const int n = hcid * NCOL + g;
-      const bool ok = n < P.ncols;
-      const int qi = ok ? n / C.R : 0;
-      const int hl = ok ? n % C.R : 0;
-      const int h = kvh * C.R + hl;
-      const int64_t qbase = b * C.qs[0] + h * C.qs[1] + qi * C.qs[2];
+      // B operand column n = g (q fetched at kernel start when vectorizable)
+      const bool ok = q_ok;
+      const int64_t qbase = q_base;
+      (void)hcid; (void)b; (void)kvh;
       float gsum[NG];
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) gsum[gi] = 0.0f;
@@ -646,10 +674,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       for (int c = 0; c < NCH; ++c) {
         float *v = vv[c];
         const int64_t qoff = qbase + (32 * c + 8 * tg) * C.qs[3];
-        if (ok && C.q_dtype == KV4_BF16 && C.qs[3] == 1 &&
-            (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(C.q) + qoff) & 15) == 0) {
-          const uint4 w = *reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(C.q) + qoff);
-          const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
+        if (q_vec) {
+          const uint32_t ws4[4] = {q_raw[c].x, q_raw[c].y, q_raw[c].z, q_raw[c].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             v[2 * e] = bf16lo_to_f32(ws4[e]);
@@ -773,6 +799,57 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       for (int e = 0; e < 4; ++e) sp_acc[gi][e] = 0.0f;
   };
 
+  // Log-sum-exp merge of nsl partial slots (slot0, slot0 + stride, ...) of
+  // this CTA's unit: into partial slot dst (dst >= 0) or into the output.
+  // Up to 8 slots' loads are in flight per round.
+  auto merge_slots = [&](int64_t slot0, int64_t stride, int nsl, int64_t dst) {
+    constexpr int D4 = D / 4;
+    for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
+      const int col = idx / D4, d4 = idx - col * D4;
+      const int n = u_hc * NCOL + col;
+      if (n >= P.ncols) continue;
+      const float4 *src = reinterpret_cast<const float4 *>(P.ws_o + (slot0 * NCOL + col) * D) + d4;
+      const float *lsrc = P.ws_lse + slot0 * NCOL + col;
+      float M = kNegInf, W = 0.0f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p0 = 0; p0 < nsl; p0 += 8) {
+        float4 v[8];
+        float lp[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int64_t pp = static_cast<int64_t>(min(p0 + e, nsl - 1)) * stride;
+          v[e] = __ldcg(src + pp * NCOL * D4);
+          lp[e] = (p0 + e < nsl) ? __ldcg(lsrc + pp * NCOL) : kNegInf;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float mn = fmaxf(M, lp[e]);
+          if (mn == kNegInf) continue;
+          const float a = exp2f(M - mn), w = exp2f(lp[e] - mn);
+          W = W * a + w;
+          acc.x = acc.x * a + w * v[e].x; acc.y = acc.y * a + w * v[e].y;
+          acc.z = acc.z * a + w * v[e].z; acc.w = acc.w * a + w * v[e].w;
+          M = mn;
+        }
+      }
+      const float inv = W > 0.0f ? 1.0f / W : 0.0f;
+      const float lse = W > 0.0f ? M + log2f(W) : kNegInf;
+      if (dst >= 0) {
+        reinterpret_cast<float4 *>(P.ws_o + (dst * NCOL + col) * D)[d4] =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (d4 == 0) P.ws_lse[dst * NCOL + col] = lse;
+      } else {
+        const int qi = n / C.R, h = u_kvh * C.R + n % C.R;
+        const int dd = 4 * d4;
+        emit_value(C, u_b, h, qi, dd, acc.x * inv);
+        emit_value(C, u_b, h, qi, dd + 1, acc.y * inv);
+        emit_value(C, u_b, h, qi, dd + 2, acc.z * inv);
+        emit_value(C, u_b, h, qi, dd + 3, acc.w * inv);
+        if (dd == 0) emit_lse(C, u_b, h, qi, lse);
+      }
+    }
+  };
+
   // Finish the CTA's unit segment: merge the 4 warps through smem, then
   // either write the output (unit wholly inside this CTA) or a partial slot;
   // the last CTA to finish a split unit (per-unit counter) merges all of the
@@ -854,56 +931,41 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
       }
     }
     if (!whole) {
-      // Bar.sync orders every thread's partial stores before thread 0's
-      // acq_rel atomic (release is cumulative); the last CTA to arrive
-      // acquires them all and merges the unit's kparts slots.
+      // Two-level merge.  Parts are grouped by MERGE_GROUP; the last CTA of a
+      // group to finish merges the group's partials (one round of loads in
+      // flight) into a group slot, and the last group merger of the unit
+      // merges the group slots into the output.  With a single group the
+      // group merger writes the output directly.  Bar.sync orders every
+      // thread's stores before thread 0's acq_rel atomic (release is
+      // cumulative); the last arriver acquires them all.
+      const int ngrp = (kparts + MERGE_GROUP - 1) / MERGE_GROUP;
+      const int grp = part / MERGE_GROUP;
+      const int gfirst = grp * MERGE_GROUP;
+      const int gsize = min(MERGE_GROUP, kparts - gfirst);
+      int *cnt_grp = P.counters - static_cast<int64_t>(P.units) * ngrp;  // [units][ngrp]
       __syncthreads();
       if (tid == 0) {
-        const int prev = atom_add_acq_rel_gpu(&P.counters[u], 1);
-        sh_last = (prev == kparts - 1);
-        if (sh_last) P.counters[u] = 0;  // re-arm for the next call
+        int *cp = ngrp > 1 ? &cnt_grp[static_cast<int64_t>(u) * ngrp + grp] : &P.counters[u];
+        const int prev = atom_add_acq_rel_gpu(cp, 1);
+        sh_last = (prev == gsize - 1);
+        if (sh_last) *cp = 0;  // re-arm for the next call
       }
       __syncthreads();
       if (sh_last) {
-        const int64_t slot0 = static_cast<int64_t>(u) * kparts;
-        for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
-          const int col = idx / D4, d4 = idx - col * D4;
-          const int n = hcid * NCOL + col;
-          if (n >= P.ncols) continue;
-          const float4 *src =
-              reinterpret_cast<const float4 *>(P.ws_o + (slot0 * NCOL + col) * D) + d4;
-          const float *lsrc = P.ws_lse + slot0 * NCOL + col;
-          // online log-sum-exp over the parts, 8 loads in flight per round
-          float M = kNegInf, W = 0.0f;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int p0 = 0; p0 < kparts; p0 += 8) {
-            float4 v[8];
-            float lp[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int p = min(p0 + e, kparts - 1);
-              v[e] = __ldcg(src + static_cast<int64_t>(p) * NCOL * D4);
-              lp[e] = (p0 + e < kparts) ? __ldcg(lsrc + static_cast<int64_t>(p) * NCOL) : kNegInf;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float mn = fmaxf(M, lp[e]);
-              if (mn == kNegInf) continue;
-              const float a = exp2f(M - mn), w = exp2f(lp[e] - mn);
-              W = W * a + w;
-              acc.x = acc.x * a + w * v[e].x; acc.y = acc.y * a + w * v[e].y;
-              acc.z = acc.z * a + w * v[e].z; acc.w = acc.w * a + w * v[e].w;
-              M = mn;
-            }
+        const int64_t gslot = static_cast<int64_t>(P.units) * kparts +
+                              static_cast<int64_t>(u) * ngrp + grp;
+        merge_slots(static_cast<int64_t>(u) * kparts + gfirst, 1, gsize, ngrp == 1 ? -1 : gslot);
+        if (ngrp > 1) {
+          __syncthreads();
+          if (tid == 0) {
+            const int prev = atom_add_acq_rel_gpu(&P.counters[u], 1);
+            sh_last = (prev == ngrp - 1);
+            if (sh_last) P.counters[u] = 0;
           }
-          const float inv = W > 0.0f ? 1.0f / W : 0.0f;
-          const int qi = n / C.R, h = kvh * C.R + n % C.R;
-          const int dd = 4 * d4;
-          emit_value(C, b, h, qi, dd, acc.x * inv);
-          emit_value(C, b, h, qi, dd + 1, acc.y * inv);
-          emit_value(C, b, h, qi, dd + 2, acc.z * inv);
-          emit_value(C, b, h, qi, dd + 3, acc.w * inv);
-          if (dd == 0) emit_lse(C, b, h, qi, W > 0.0f ? M + log2f(W) : kNegInf);
+          __syncthreads();
+          if (sh_last)
+            merge_slots(static_cast<int64_t>(P.units) * kparts + static_cast<int64_t>(u) * ngrp,
+                        1, ngrp, -1);
         }
       }
     }
@@ -1185,7 +1247,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : 3))
     __syncwarp();
     if (lane == 0) {
       uint32_t old;
-      asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+      asm volatile(KV4_RELEASE_ATOM " %0, [%1], 1;"
                    : "=r"(old)
                    : "r"(smem_u32(&sh_done[stage]))
                    : "memory");
@@ -1391,6 +1453,24 @@ static int fast_occupancy(int D, int G, int sdt, bool split) {
   return 1;
 }
 
+// Split-K workspace: partial slots [units * parts] then first-level group
+// slots [units * groups] (more than one group only), each NCOL x (D + 1)
+// floats; the counters sit at the END of the caller's buffer: [units][groups]
+// first-level counters, then [units] unit counters.
+static int merge_groups(int parts) {
+  const int g = (parts + MERGE_GROUP - 1) / MERGE_GROUP;
+  return g > 1 ? g : 0;
+}
+static size_t counter_bytes_of(int units, int parts) {
+  return static_cast<size_t>(units) * (1 + merge_groups(parts)) * sizeof(int);
+}
+static size_t ws_bytes_of(int units, int parts, int D) {
+  if (parts <= 1) return 0;
+  const size_t slots = static_cast<size_t>(units) * (parts + merge_groups(parts));
+  return (counter_bytes_of(units, parts) + 15) / 16 * 16 +
+         slots * NCOL * (static_cast<size_t>(D) + 1) * sizeof(float);
+}
+
 static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
                       const kv4_tensor *vp, const kv4_tensor *vs, const Shape &S,
                       const kv4_attn_opts *opts, Plan &pl) {
@@ -1422,10 +1502,7 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     pl.L = static_cast<int>((pl.tpu + k - 1) / k);
     pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
     pl.need_merge = k > 1;
-    pl.ws_bytes = pl.need_merge ? (static_cast<size_t>(pl.units) * sizeof(int) + 15) / 16 * 16 +
-                                      static_cast<size_t>(pl.units) * pl.maxp * NCOL *
-                                      (static_cast<size_t>(pl.D) + 1) * sizeof(float)
-                                : 0;
+    pl.ws_bytes = ws_bytes_of(pl.units, pl.maxp, pl.D);
   } else {
     pl.path = 2;
     pl.ws_bytes = 0;
@@ -1600,10 +1677,7 @@ static void set_parts(Plan &pl, int64_t k) {
   pl.L = static_cast<int>((pl.tpu + k - 1) / k);
   pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
   pl.need_merge = k > 1;
-  pl.ws_bytes = pl.need_merge ? (static_cast<size_t>(pl.units) * sizeof(int) + 15) / 16 * 16 +
-                                    static_cast<size_t>(pl.units) * pl.maxp * NCOL *
-                                        (static_cast<size_t>(pl.D) + 1) * sizeof(float)
-                              : 0;
+  pl.ws_bytes = ws_bytes_of(pl.units, pl.maxp, pl.D);
 }
 
 // paged: keep each CTA's block-table slice within 48 KB of shared memory
@@ -1753,7 +1827,9 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
                                     static_cast<char *>(ws) +
                                     ((ws_bytes - static_cast<size_t>(pl.units) * 4) & ~size_t(3)))
                               : nullptr;
-    FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) * pl.maxp * NCOL * pl.D
+    FP.units = pl.units;
+    FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) *
+                                            (pl.maxp + merge_groups(pl.maxp)) * NCOL * pl.D
                             : nullptr;
     if (pl.sdt == KV4_BF16) return launch_fast_st<__nv_bfloat16>(FP, pl, kp, ks, vp, vs, st);
     if (pl.sdt == KV4_F16) return launch_fast_st<__half>(FP, pl, kp, ks, vp, vs, st);
@@ -1973,7 +2049,7 @@ extern "C" int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_pa
   if (plan.workspace_bytes == 0)  // nothing to scratch: identical to kv4_attention
     return kv4_attention(q, k_packed, k_scales, v_packed, v_scales, out, group_size, is_causal,
                          sm_scale, nullptr, 0, nullptr, stream);
-  const size_t counters = static_cast<size_t>(plan.units) * 4;
+  const size_t counters = counter_bytes_of(plan.units, plan.max_parts);
   const size_t data = static_cast<size_t>(plan.workspace_bytes) - ((counters + 15) / 16 * 16);
   if (counters > kNoAllocCounterBytes || data > kNoAllocScratchBytes - kNoAllocCounterBytes)
     return KV4_ERR_SCRATCH_LIMIT;

@@ -114,7 +114,9 @@ def _workspace(dev: torch.device, plan: AttnPlan) -> torch.Tensor | None:
     nbytes = int(plan.workspace_bytes)
     if nbytes <= 0:
         return None
-    counters = (int(plan.units) * 4 + 15) // 16 * 16
+    # unit counters plus first-level merge-group counters (8 parts per group)
+    groups = (int(plan.max_parts) + 7) // 8
+    counters = (int(plan.units) * 4 * (1 + (groups if groups > 1 else 0)) + 15) // 16 * 16
     data = nbytes - counters
     reserve = max(_COUNTER_RESERVE, counters)
     key = (dev.index, _stream(dev))
