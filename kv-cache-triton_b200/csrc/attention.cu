@@ -453,10 +453,14 @@ __device__ __forceinline__ void scales_row(uint32_t addr, float (&s)[NG]) {
   }
 }
 
-template <int D, int G, typename ST, bool SPLIT, bool PAGED>
+// MODE: 0 = bf16 q; 1 = fp16/fp32 q as a hi/lo pair (SPLIT); 2 = bf16 q with
+// at most 4 columns per KV head, paired into the 8 MMA columns (PAIR)
+template <int D, int G, typename ST, int MODE, bool PAGED>
 __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     kv4_attn_fast(const FastParams P, const __grid_constant__ CUtensorMap tm_kp,
                   const __grid_constant__ CUtensorMap tm_vp) {
+  constexpr bool SPLIT = MODE == 1;
+  constexpr bool PAIR = MODE == 2;
   using Cfg = FastCfg<D, G, ST>;
   constexpr int NCH = Cfg::NCH, NG = Cfg::NG, CPG = Cfg::CPG;
   const AttnCommon &C = P.c;
@@ -504,7 +508,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
 
   // q of this lane's B-operand column (n = g), requested before anything
   // else so that it is not queued behind the CTA's tile loads in HBM
-  const int q_n = u_hc * NCOL + g;
+  const int q_n = u_hc * NCOL + (PAIR ? (g & 3) : g);
   const bool q_ok = q_n < P.ncols;
   const int64_t q_base = q_ok ? u_b * C.qs[0] + (u_kvh * C.R + q_n % C.R) * C.qs[1] +
                                     (q_n / C.R) * C.qs[2]
@@ -650,7 +654,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
 
   // ---- per-unit state --------------------------------------------------
   uint32_t qf[NCH][2][2];               // q B-fragments (hi), [chunk][kstep][reg]
-  uint32_t qfl[SPLIT ? NCH : 1][2][2];  // lo parts (SPLIT only)
+  uint32_t qfl[(SPLIT || PAIR) ? NCH : 1][2][2];  // SPLIT: lo parts; PAIR: slab-1 fragments
   float o_acc[NCH][2][4];               // O^T fragments [chunk][j][c]
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
@@ -746,6 +750,17 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
                             f16lo_to_f32(qf[c][1][1]) + f16hi_to_f32(qf[c][1][1]);
           gsum[c / CPG] += -1032.0f * b1 - 1152.0f * b16;
         }
+        if constexpr (PAIR) {  // slab 0 runs against lanes g < 4, slab 1 against g >= 4
+#pragma unroll
+          for (int c = 0; c < NCH; ++c)
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                qfl[c][k][j] = g >= 4 ? qf[c][k][j] : 0u;
+                qf[c][k][j] = g < 4 ? qf[c][k][j] : 0u;
+              }
+        }
       }
       // reduce the per-group sums over the 4 lanes of the quad (tg)
 #pragma unroll
@@ -769,7 +784,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int n = hcid * NCOL + 2 * tg + j;
+      const int n = hcid * NCOL + (PAIR ? ((2 * tg + j) & 3) : 2 * tg + j);
       const int qi = n < P.ncols ? n / C.R : 0;
       int64_t lim = sk_u;
       if (C.causal) {
@@ -783,8 +798,9 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     }
     {
       // padding columns (n >= ncols) never mask real ones: treat them as unlimited
-      const int a = (hcid * NCOL + 2 * tg < P.ncols) ? col_lim[0] : INT_MAX;
-      const int b2 = (hcid * NCOL + 2 * tg + 1 < P.ncols) ? col_lim[1] : INT_MAX;
+      const int n0 = hcid * NCOL + (PAIR ? ((2 * tg) & 3) : 2 * tg);
+      const int a = (n0 < P.ncols) ? col_lim[0] : INT_MAX;
+      const int b2 = (n0 + 1 < P.ncols) ? col_lim[1] : INT_MAX;
       lim_min = __reduce_min_sync(0xffffffffu, min(a, b2));
     }
 #pragma unroll
@@ -857,7 +873,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
   auto flush = [&]() {
     const int hcid = u_hc, b = u_b, kvh = u_kvh;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {  // l over the 8 token-row lanes
+    for (int j = 0; j < 2; ++j) {  // l over the 8 token-row lanes (PAIR: and both slabs)
+      if constexpr (PAIR) l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 2);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
@@ -914,7 +931,12 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
       float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int w = 0; w < NWARP; ++w) {
-        const float4 x = *reinterpret_cast<const float4 *>(&merge_o[(w * NCOL + col) * D + 4 * d4]);
+        float4 x = *reinterpret_cast<const float4 *>(&merge_o[(w * NCOL + col) * D + 4 * d4]);
+        if constexpr (PAIR) {  // column col + 4 holds the same q column's slab-1 rows
+          const float4 y =
+              *reinterpret_cast<const float4 *>(&merge_o[(w * NCOL + col + 4) * D + 4 * d4]);
+          x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
+        }
         const float f = merge_f[w * NCOL + col];
         val.x += f * x.x; val.y += f * x.y; val.z += f * x.z; val.w += f * x.w;
       }
@@ -1034,6 +1056,165 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
     }
+    if constexpr (PAIR) {
+      // ---- paired columns (at most 4 q columns per KV head) ---------------
+      // The 8 MMA columns hold the 4 columns twice: columns 0-3 score the
+      // warp's rows 0-15 (slab 0), columns 4-7 its rows 16-31 (slab 1), by
+      // running slab 0 against q in lanes g < 4 only (qfA) and slab 1
+      // against q in lanes g >= 4 only (qfB) into ONE accumulator.  Every
+      // accumulator element is then a real (token, column) pair: lane
+      // (g, tg) holds rows g, g+8 of slab tg / 2 for columns 2tg, 2tg+1
+      // (column c is q column c & 3).
+      const int slab = tg >> 1;
+      const int rbase = WROWS * warp + 16 * slab + g;  // the lane's rows: rbase, rbase + 8
+      float s2[2][2] = {};
+      SRow<NG, ST> krow2[2];
+      krow2[0].load(ksb + rbase * Cfg::SROW);
+      krow2[1].load(ksb + (rbase + 8) * Cfg::SROW);
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        float acc[4];
+#pragma unroll
+        for (int cc = 0; cc < CPG; ++cc) {
+          const int c = gi * CPG + cc;
+          uint32_t xr[4];  // rows g, g+8 of slab 0, then of slab 1
+          ldsm_x4(kp + k_off[c], xr);
+          const uint32_t y0 = xr[0] >> 8, y1 = xr[1] >> 8, y2 = xr[2] >> 8, y3 = xr[3] >> 8;
+          if (cc == 0) {
+            float bq[4];
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(bq[0]), "=f"(bq[1]), "=f"(bq[2]), "=f"(bq[3])
+                         : "r"(bias_s + ((warp * NG + gi) * 4 + tg) * 16));
+            mma_f16_16816_c(acc, h_lo(xr[0]), h_lo(xr[1]), h_hi(xr[0]), h_hi(xr[1]),
+                            qf[c][0][0], qf[c][0][1], bq[0], bq[1], bq[2], bq[3]);
+          } else {
+            mma_f16_16816(acc, h_lo(xr[0]), h_lo(xr[1]), h_hi(xr[0]), h_hi(xr[1]), qf[c][0][0],
+                          qf[c][0][1]);
+          }
+          mma_f16_16816(acc, h_lo(y0), h_lo(y1), h_hi(y0), h_hi(y1), qf[c][1][0], qf[c][1][1]);
+          mma_f16_16816(acc, h_lo(xr[2]), h_lo(xr[3]), h_hi(xr[2]), h_hi(xr[3]), qfl[c][0][0],
+                        qfl[c][0][1]);
+          mma_f16_16816(acc, h_lo(y2), h_lo(y3), h_hi(y2), h_hi(y3), qfl[c][1][0], qfl[c][1][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const float ks = krow2[r].get(gi);
+          s2[r][0] = fmaf(ks, acc[2 * r], s2[r][0]);
+          s2[r][1] = fmaf(ks, acc[2 * r + 1], s2[r][1]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        s2[r][0] *= col_inv[0];
+        s2[r][1] *= col_inv[1];
+      }
+      const int tokr = tok0 + 16 * slab + g;  // token of row 0 (row 1: + 8)
+      if (tok0 + WROWS > lim_min) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int t = tokr + 8 * r;
+          if (t >= col_lim[0]) s2[r][0] = kNegInf;
+          if (t >= col_lim[1]) s2[r][1] = kNegInf;
+          if (t >= sk_u && (tg & 1) == 0) {  // zero the row's V scales (see below)
+            const uint32_t row = vsb + (rbase + 8 * r) * Cfg::SROW;
+#pragma unroll
+            for (int e = 0; e < Cfg::SROW / 2; ++e)
+              asm volatile("st.shared.u16 [%0], %1;" ::"r"(row + 2 * e), "r"(0u) : "memory");
+          }
+        }
+      }
+      if (tok0 + WROWS > sk_u) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+      }
+      // online softmax: column c's 32 rows are in lanes with tg = c/2 and
+      // c/2 + 2 (xor 2), all g (xor 4, 8, 16)
+      float mx[2];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        mx[cc] = fmaxf(s2[0][cc], s2[1][cc]);
+        mx[cc] = fmaxf(mx[cc], __shfl_xor_sync(0xffffffffu, mx[cc], 2));
+#pragma unroll
+        for (int o = 4; o <= 16; o <<= 1)
+          mx[cc] = fmaxf(mx[cc], __shfl_xor_sync(0xffffffffu, mx[cc], o));
+      }
+      const bool need = (mx[0] > m_run[0] + 8.0f) || (mx[1] > m_run[1] + 8.0f);
+      if (__any_sync(0xffffffffu, need)) {
+        float alpha[2];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const float mn = fmaxf(m_run[cc], mx[cc]);
+          alpha[cc] = (mn == kNegInf) ? 1.0f : fast_exp2(m_run[cc] - mn);
+          m_run[cc] = mn;
+          l_run[cc] *= alpha[cc];
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            o_acc[c][j][0] *= alpha[0];
+            o_acc[c][j][1] *= alpha[1];
+            o_acc[c][j][2] *= alpha[0];
+            o_acc[c][j][3] *= alpha[1];
+          }
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          sp_acc[gi][0] *= alpha[0];
+          sp_acc[gi][1] *= alpha[1];
+          sp_acc[gi][2] *= alpha[0];
+          sp_acc[gi][3] *= alpha[1];
+        }
+      }
+      const float me[2] = {(m_run[0] == kNegInf) ? 0.0f : m_run[0],
+                           (m_run[1] == kNegInf) ? 0.0f : m_run[1]};
+      float p2[2][2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          p2[r][cc] = fast_exp2(s2[r][cc] - me[cc]);
+          l_run[cc] += p2[r][cc];
+        }
+      // P' = P * v_scale (fp32, one rounding to bf16), transposed into the B
+      // layout: lane (g, tg) then holds column g; slab 0's MMAs take the
+      // columns g < 4 (mask_a), slab 1's the columns g >= 4 (mask_b)
+      uint32_t pb[NG][2];
+      {
+        SRow<NG, ST> va, vc;
+        va.load(vsb + rbase * Cfg::SROW);
+        vc.load(vsb + (rbase + 8) * Cfg::SROW);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          const float vs0 = va.get(gi), vs1 = vc.get(gi);
+          pb[gi][0] = movmatrix_trans(pack_bf16x2(p2[0][0] * vs0, p2[0][1] * vs0));
+          pb[gi][1] = movmatrix_trans(pack_bf16x2(p2[1][0] * vs1, p2[1][1] * vs1));
+        }
+      }
+      const uint32_t mask_a = g < 4 ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t msk = h == 0 ? mask_a : ~mask_a;
+#pragma unroll
+        for (int cp = 0; cp < NCH / 2; ++cp) {
+          uint32_t wr[4];
+          ldsm_x4_trans(vp + m_off[cp] + h * 16 * P_, wr);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 2 * cp + e;
+            const int gi = c / CPG;
+            const uint32_t b0 = pb[gi][0] & msk, b1 = pb[gi][1] & msk;
+            const uint32_t wab = wr[2 * e], wcd = wr[2 * e + 1];
+            const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
+            const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
+            mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, b0, b1);
+            mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, b0, b1);
+          }
+        }
+      }
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi)
+        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
+    } else {
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
     // Per scale group: partial dot products on the tensor cores (the first
     // MMA of a group takes the -136*sum(q) bias as its C input), then the
@@ -1239,6 +1420,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
       }
     }
 
+    }  // PAIR / unpaired
+
     // ---------------- release the stage, refill, flush at unit end ------
     // Each warp counts itself out of the stage (acq_rel: its reads of the
     // stage happen before); the LAST warp to finish refills it at once, so
@@ -1356,6 +1539,7 @@ struct Plan {
   int path;  // 1 fast, 2 generic
   int D, sdt;
   bool split;
+  int mode;  // kernel MODE: 0 bf16 q, 1 split q, 2 paired columns
   int hc, ncols, tpu, L, maxp, ctas, units;
   int64_t total_tiles;
   size_t ws_bytes;
@@ -1399,7 +1583,7 @@ static int current_device() {
 // Occupancy of a fast-path instantiation on the current device.  The dynamic
 // shared-memory attribute is per device (per context), so it is set, and the
 // occupancy queried, once for every device that launches the kernel.
-template <int D, int G, typename ST, bool SPLIT, bool PAGED = false>
+template <int D, int G, typename ST, int MODE, bool PAGED = false>
 static int occupancy_of() {
   static std::atomic<int> occ[64];
   static std::mutex mu;
@@ -1409,10 +1593,10 @@ static int occupancy_of() {
   std::lock_guard<std::mutex> lock(mu);
   if ((o = occ[dev].load(std::memory_order_relaxed)) > 0) return o;
   using Cfg = FastCfg<D, G, ST>;
-  cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
+  cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, MODE, PAGED>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
   o = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, SPLIT, PAGED>, 128,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kv4_attn_fast<D, G, ST, MODE, PAGED>, 128,
                                                     Cfg::SMEM) != cudaSuccess ||
       o < 1)
     o = 1;
@@ -1432,15 +1616,11 @@ static int sm_count() {  // per device, queried once
   return n;
 }
 
-template <int D, int G, typename ST, bool SPLIT, typename F>
-static auto with_occ(F &&f) {
-  return f(occupancy_of<D, G, ST, SPLIT>());
-}
-
-static int fast_occupancy(int D, int G, int sdt, bool split) {
-#define KV4_OCC(DD, GG, STT)                                                         \
-  if (D == DD && G == GG) return split ? occupancy_of<DD, GG, STT, true>()           \
-                                       : occupancy_of<DD, GG, STT, false>();
+static int fast_occupancy(int D, int G, int sdt, int mode) {
+#define KV4_OCC(DD, GG, STT)                                                     \
+  if (D == DD && G == GG)                                                        \
+    return mode == 1 ? occupancy_of<DD, GG, STT, 1>()                            \
+                     : (mode == 2 ? occupancy_of<DD, GG, STT, 2>() : occupancy_of<DD, GG, STT, 0>());
 #define KV4_OCC_S(STT)                                                               \
   KV4_OCC(64, 32, STT) KV4_OCC(64, 64, STT) KV4_OCC(128, 32, STT) KV4_OCC(128, 64, STT) \
       KV4_OCC(128, 128, STT) KV4_OCC(256, 32, STT) KV4_OCC(256, 64, STT)              \
@@ -1487,7 +1667,8 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     pl.units = static_cast<int>(S.B * S.Hkv * pl.hc);
     pl.tpu = static_cast<int>((S.sk + TOK - 1) / TOK);
     pl.total_tiles = static_cast<int64_t>(pl.units) * pl.tpu;
-    const int occ = fast_occupancy(pl.D, S.G, pl.sdt, pl.split);
+    pl.mode = pl.split ? 1 : (pl.ncols <= 4 ? 2 : 0);
+    const int occ = fast_occupancy(pl.D, S.G, pl.sdt, pl.mode);
     int64_t target = static_cast<int64_t>(sm_count()) * occ;
     if (opts && opts->max_ctas > 0) target = std::min<int64_t>(target, opts->max_ctas);
     // split-K: kparts CTAs per unit, as many as fit one wave of resident CTAs
@@ -1571,7 +1752,7 @@ static int encode_packed_cached(CUtensorMap *tm, const kv4_tensor *t, int row_by
   return KV4_OK;
 }
 
-template <int D, int G, typename ST, bool SPLIT, bool PAGED>
+template <int D, int G, typename ST, int MODE, bool PAGED>
 static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
                          cudaStream_t st) {
@@ -1581,7 +1762,7 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
   const int box_rows = FP.page > 0 ? FP.page : TOK;  // paged: one box per page
   if ((rc = encode_packed_cached(&tkp, kp, Cfg::P, box_rows))) return rc;
   if ((rc = encode_packed_cached(&tvp, vp, Cfg::P, box_rows))) return rc;
-  occupancy_of<D, G, ST, SPLIT, PAGED>();  // sets the smem attribute once
+  occupancy_of<D, G, ST, MODE, PAGED>();  // sets the smem attribute once
   int smem = Cfg::SMEM;
   if (FP.page > 0) {  // room for the block-table slice after the staged append row
     smem += 16 + FP.bt_slots * 4;
@@ -1592,14 +1773,14 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
       static std::mutex mu;
       std::lock_guard<std::mutex> lock(mu);
       if (smem > smem_set[dev].load(std::memory_order_relaxed)) {
-        rc = cuda_status(cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, SPLIT, PAGED>,
+        rc = cuda_status(cudaFuncSetAttribute(kv4_attn_fast<D, G, ST, MODE, PAGED>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         if (rc) return rc;
         smem_set[dev].store(smem, std::memory_order_release);
       }
     }
   }
-  kv4_attn_fast<D, G, ST, SPLIT, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
+  kv4_attn_fast<D, G, ST, MODE, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
   return rc;
@@ -1609,11 +1790,14 @@ template <int D, int G, typename ST>
 static int launch_fast_s(const FastParams &FP, const Plan &pl, const kv4_tensor *kp,
                          const kv4_tensor *ks, const kv4_tensor *vp, const kv4_tensor *vs,
                          cudaStream_t st) {
-  if (FP.page > 0)
-    return pl.split ? launch_fast_t<D, G, ST, true, true>(FP, pl, kp, ks, vp, vs, st)
-                    : launch_fast_t<D, G, ST, false, true>(FP, pl, kp, ks, vp, vs, st);
-  return pl.split ? launch_fast_t<D, G, ST, true, false>(FP, pl, kp, ks, vp, vs, st)
-                  : launch_fast_t<D, G, ST, false, false>(FP, pl, kp, ks, vp, vs, st);
+  if (FP.page > 0) {
+    if (pl.mode == 1) return launch_fast_t<D, G, ST, 1, true>(FP, pl, kp, ks, vp, vs, st);
+    if (pl.mode == 2) return launch_fast_t<D, G, ST, 2, true>(FP, pl, kp, ks, vp, vs, st);
+    return launch_fast_t<D, G, ST, 0, true>(FP, pl, kp, ks, vp, vs, st);
+  }
+  if (pl.mode == 1) return launch_fast_t<D, G, ST, 1, false>(FP, pl, kp, ks, vp, vs, st);
+  if (pl.mode == 2) return launch_fast_t<D, G, ST, 2, false>(FP, pl, kp, ks, vp, vs, st);
+  return launch_fast_t<D, G, ST, 0, false>(FP, pl, kp, ks, vp, vs, st);
 }
 
 template <typename ST>
