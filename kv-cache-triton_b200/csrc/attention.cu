@@ -203,6 +203,7 @@ struct FastParams {
   int *counters;  // [units] finished-segment counts (zero between calls); the
                   // [units][ngroups] first-level counters sit right before
   int units;
+  int cs;         // > 1: launched as clusters of cs CTAs (consecutive parts of a unit)
   const char *ks, *vs;         // scale tensors
   int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
   // Fused quantize-on-append (app_row >= 0): the new token's K/V rows
@@ -331,7 +332,7 @@ struct FastCfg {
 #define KV4_MINB 3
 #endif
   static constexpr int STAGES = (D == 256) ? 2 : KV4_STAGES;
-  static constexpr int MERGE = NWARP * NCOL * D * 4;
+  static constexpr int MERGE = (NWARP + 1) * NCOL * D * 4;  // per-warp o + the CTA's o
   static_assert(MERGE <= STAGES * STAGE, "merge buffer aliases the stages");
   static constexpr int APP = 2 * P + 2 * SROW;  // staged new row (fused append)
   static constexpr int BIAS = NWARP * NG * 4 * 16;  // per warp: [group][tg] C quads
@@ -504,7 +505,8 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     sk_u = sl < 0 ? 0 : (sl < C.sk ? sl : C.sk);
   }
   const int ntiles = max(0, min(t_end, (sk_u + TOK - 1) / TOK) - t_begin);
-  if (ntiles <= 0 && !paged) return;
+  // (a CTA of a cluster never leaves early: its cluster waits for it at the merge)
+  if (ntiles <= 0 && !paged && P.cs <= 1) return;
 
   // q of this lane's B-operand column (n = g), requested before anything
   // else so that it is not queued behind the CTA's tile loads in HBM
@@ -818,9 +820,11 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
   // Log-sum-exp merge of nsl partial slots (slot0, slot0 + stride, ...) of
   // this CTA's unit: into partial slot dst (dst >= 0) or into the output.
   // Up to 8 slots' loads are in flight per round.
-  auto merge_slots = [&](int64_t slot0, int64_t stride, int nsl, int64_t dst) {
+  auto merge_slots = [&](int64_t slot0, int64_t stride, int nsl, int64_t dst, int first = 0,
+                         int step = 1) {
     constexpr int D4 = D / 4;
-    for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
+    for (int idx = first * static_cast<int>(blockDim.x) + tid; idx < NCOL * D4;
+         idx += step * static_cast<int>(blockDim.x)) {
       const int col = idx / D4, d4 = idx - col * D4;
       const int n = u_hc * NCOL + col;
       if (n >= P.ncols) continue;
@@ -924,6 +928,9 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     }
     __syncthreads();
     constexpr int D4 = D / 4;
+    const int cs = P.cs;  // > 1: the unit's parts are clusters of cs CTAs
+    // the CTA's own partial (o normalised, lse) for the cluster merge
+    float *cta_o = merge_o + NWARP * NCOL * D;
     for (int idx = tid; idx < NCOL * D4; idx += blockDim.x) {
       const int col = idx / D4, d4 = idx - col * D4;
       const int n = hcid * NCOL + col;
@@ -947,12 +954,87 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
         emit_value(C, b, h, qi, 4 * d4 + 2, val.z);
         emit_value(C, b, h, qi, 4 * d4 + 3, val.w);
         if (d4 == 0) emit_lse(C, b, h, qi, merge_lse[col]);
+      } else if (cs > 1) {
+        *reinterpret_cast<float4 *>(&cta_o[col * D + 4 * d4]) = val;
       } else {
         reinterpret_cast<float4 *>(P.ws_o + (static_cast<int64_t>(slot) * NCOL + col) * D)[d4] = val;
         if (d4 == 0) P.ws_lse[static_cast<int64_t>(slot) * NCOL + col] = merge_lse[col];
       }
     }
-    if (!whole) {
+    if (!whole && cs > 1) {
+      // Cluster merge: the cs CTAs of a cluster are consecutive parts of the
+      // unit; each reads the cs partials from the CTAs' shared memory
+      // (distributed shared memory) for its slice of the outputs.  With one
+      // cluster per unit that is the output; otherwise the slices form the
+      // cluster's group slot in global memory, and the last cluster of the
+      // unit to finish (per-unit counter) merges the group slots.
+      const int rank = static_cast<int>(cluster_ctarank());
+      const int ngrp = kparts / cs, grp = part / cs;
+      const int64_t gslot0 = static_cast<int64_t>(P.units) * kparts + static_cast<int64_t>(u) * ngrp;
+      cluster_sync();
+      for (int idx = rank * static_cast<int>(blockDim.x) + tid; idx < NCOL * D4;
+           idx += cs * static_cast<int>(blockDim.x)) {
+        const int col = idx / D4, d4 = idx - col * D4;
+        const int n = hcid * NCOL + col;
+        if (n >= P.ncols) continue;
+        const uint32_t ao = smem_u32(&cta_o[col * D + 4 * d4]);
+        const uint32_t al = smem_u32(&merge_lse[col]);
+        float4 v[8];
+        float lp[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q < cs) {
+            v[q] = ld_dsmem_f4(dsmem_addr(ao, q));
+            lp[q] = ld_dsmem_f32(dsmem_addr(al, q));
+          }
+        }
+        float M = kNegInf;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < cs) M = fmaxf(M, lp[q]);
+        float W = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != kNegInf) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (q < cs) {
+              const float w = exp2f(lp[q] - M);
+              W += w;
+              acc.x += w * v[q].x; acc.y += w * v[q].y; acc.z += w * v[q].z; acc.w += w * v[q].w;
+            }
+          }
+        }
+        const float inv = W > 0.0f ? 1.0f / W : 0.0f;
+        const float lse = W > 0.0f ? M + log2f(W) : kNegInf;
+        if (ngrp == 1) {
+          const int qi = n / C.R, h = kvh * C.R + n % C.R;
+          emit_value(C, b, h, qi, 4 * d4, acc.x * inv);
+          emit_value(C, b, h, qi, 4 * d4 + 1, acc.y * inv);
+          emit_value(C, b, h, qi, 4 * d4 + 2, acc.z * inv);
+          emit_value(C, b, h, qi, 4 * d4 + 3, acc.w * inv);
+          if (d4 == 0) emit_lse(C, b, h, qi, lse);
+        } else {
+          const int64_t gs = gslot0 + grp;
+          reinterpret_cast<float4 *>(P.ws_o + (gs * NCOL + col) * D)[d4] =
+              make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+          if (d4 == 0) P.ws_lse[gs * NCOL + col] = lse;
+        }
+      }
+      if (ngrp > 1) __threadfence();  // group-slot stores before the cluster's release below
+      cluster_sync();  // every read of another CTA's shared memory is done
+      if (ngrp > 1) {
+        if (rank == 0 && tid == 0) {
+          const int prev = atom_add_acq_rel_gpu(&P.counters[u], 1);
+          sh_last = (prev == ngrp - 1);
+          if (sh_last) P.counters[u] = 0;  // re-arm for the next call
+        }
+        cluster_sync();
+        const int last = ld_dsmem_s32(dsmem_addr(smem_u32(&sh_last), 0));
+        cluster_sync();  // rank 0's flag is read before any CTA exits
+        if (last) merge_slots(gslot0, 1, ngrp, -1, rank, cs);
+      }
+    }
+    if (!whole && cs <= 1) {
       // Two-level merge.  Parts are grouped by MERGE_GROUP; the last CTA of a
       // group to finish merges the group's partials (one round of loads in
       // flight) into a group slot, and the last group merger of the unit
@@ -1540,6 +1622,7 @@ struct Plan {
   int D, sdt;
   bool split;
   int mode;  // kernel MODE: 0 bf16 q, 1 split q, 2 paired columns
+  int cs;    // cluster size of the split-K merge (1: no clusters)
   int hc, ncols, tpu, L, maxp, ctas, units;
   int64_t total_tiles;
   size_t ws_bytes;
@@ -1651,6 +1734,15 @@ static size_t ws_bytes_of(int units, int parts, int D) {
          slots * NCOL * (static_cast<size_t>(D) + 1) * sizeof(float);
 }
 
+// Split-K parts of a unit merge inside one thread-block cluster (through
+// distributed shared memory) when there are at most kMaxCluster of them;
+// more parts merge through global memory in two levels (measured: clusters
+// of 8 plus a global level were slower than the global two-level merge).
+constexpr int kMaxCluster = 8;
+static int cluster_size_of(int64_t k) {
+  return static_cast<int>(k > 1 && k <= kMaxCluster ? k : 1);
+}
+
 static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tensor *ks,
                       const kv4_tensor *vp, const kv4_tensor *vs, const Shape &S,
                       const kv4_attn_opts *opts, Plan &pl) {
@@ -1679,6 +1771,7 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     k = std::min<int64_t>(k, std::max<int64_t>(1, pl.tpu / 4));
     if (opts && opts->tiles_per_cta > 0) k = (pl.tpu + opts->tiles_per_cta - 1) / opts->tiles_per_cta;
     k = std::min<int64_t>(k, pl.tpu);
+    pl.cs = cluster_size_of(k);
     pl.maxp = static_cast<int>(k);
     pl.L = static_cast<int>((pl.tpu + k - 1) / k);
     pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
@@ -1780,7 +1873,24 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
       }
     }
   }
-  kv4_attn_fast<D, G, ST, MODE, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
+  if (FP.cs > 1) {  // the split-K parts of a unit merge inside a thread-block cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.ctas));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(FP.cs);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    rc = cuda_status(cudaLaunchKernelEx(&cfg, kv4_attn_fast<D, G, ST, MODE, PAGED>, FP, tkp, tvp));
+    if (rc) return rc;
+  } else {
+    kv4_attn_fast<D, G, ST, MODE, PAGED><<<pl.ctas, 128, smem, st>>>(FP, tkp, tvp);
+  }
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
   return rc;
@@ -1857,6 +1967,7 @@ static int validate_paged(const kv4_tensor *q, const kv4_tensor *kp, const kv4_t
 // Recompute the split-dependent fields of a fast plan for kparts = k.
 static void set_parts(Plan &pl, int64_t k) {
   k = std::max<int64_t>(1, std::min<int64_t>(k, pl.tpu));
+  pl.cs = cluster_size_of(k);
   pl.maxp = static_cast<int>(k);
   pl.L = static_cast<int>((pl.tpu + k - 1) / k);
   pl.ctas = static_cast<int>(static_cast<int64_t>(pl.units) * k);
@@ -2012,6 +2123,7 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
                                     ((ws_bytes - static_cast<size_t>(pl.units) * 4) & ~size_t(3)))
                               : nullptr;
     FP.units = pl.units;
+    FP.cs = pl.cs;
     FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) *
                                             (pl.maxp + merge_groups(pl.maxp)) * NCOL * pl.D
                             : nullptr;
