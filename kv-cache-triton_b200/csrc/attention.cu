@@ -661,6 +661,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
   float col_inv[2];  // score factor of columns 2tg, 2tg+1 (log2 domain)
+  int vexp = 0;      // PAIR: per-warp power-of-two factor of the f16 P'' (see below)
   int col_lim[2];
   int lim_min = 0;  // smallest key limit over the CTA's columns (warp-uniform)
 
@@ -902,9 +903,19 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
         const int d0 = 32 * c + 4 * g + 2 * j;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {  // column 2tg + cc
-          const float corr = 136.0f * sp_acc[gi][cc];
-          *reinterpret_cast<float2 *>(&mo[(2 * tg + cc) * D + d0]) =
-              make_float2(o_acc[c][j][cc] - corr, o_acc[c][j][2 + cc] - corr);
+          if constexpr (PAIR) {
+            // f16 V operands: even dims hold 1024 + code, odd dims 1024 + 16 code;
+            // undo the warp's 2^vexp factor
+            const float sp = sp_acc[gi][cc];
+            const float ivf = __int_as_float((127 - vexp) << 23);
+            *reinterpret_cast<float2 *>(&mo[(2 * tg + cc) * D + d0]) =
+                make_float2((o_acc[c][j][cc] - 1032.0f * sp) * ivf,
+                            (o_acc[c][j][2 + cc] * 0.0625f - 72.0f * sp) * ivf);
+          } else {
+            const float corr = 136.0f * sp_acc[gi][cc];
+            *reinterpret_cast<float2 *>(&mo[(2 * tg + cc) * D + d0]) =
+                make_float2(o_acc[c][j][cc] - corr, o_acc[c][j][2 + cc] - corr);
+          }
         }
       }
     }
@@ -1257,19 +1268,53 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
           p2[r][cc] = fast_exp2(s2[r][cc] - me[cc]);
           l_run[cc] += p2[r][cc];
         }
-      // P' = P * v_scale (fp32, one rounding to bf16), transposed into the B
-      // layout: lane (g, tg) then holds column g; slab 0's MMAs take the
-      // columns g < 4 (mask_a), slab 1's the columns g >= 4 (mask_b)
+      // P'' = P * v_scale * 2^vexp in fp32, one rounding to f16 (V codes
+      // enter the MMAs as f16 magic-number operands, 5 integer ops per 8
+      // codes), transposed into the B layout: lane (g, tg) then holds column
+      // g; slab 0's MMAs take the columns g < 4, slab 1's the columns g >= 4.
+      // vexp is a per-warp power-of-two exponent that keeps the step's
+      // largest V scale times 2^vexp within [2^-6, 2^6], so P'' (P <= 2^8)
+      // stays inside the f16 range with full precision; when a step falls
+      // outside, vexp moves and the accumulators are rescaled exactly.
       uint32_t pb[NG][2];
       {
         SRow<NG, ST> va, vc;
         va.load(vsb + rbase * Cfg::SROW);
         vc.load(vsb + (rbase + 8) * Cfg::SROW);
+        float vs0[NG], vs1[NG];
+        float vmax = 0.0f;
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
-          const float vs0 = va.get(gi), vs1 = vc.get(gi);
-          pb[gi][0] = movmatrix_trans(pack_bf16x2(p2[0][0] * vs0, p2[0][1] * vs0));
-          pb[gi][1] = movmatrix_trans(pack_bf16x2(p2[1][0] * vs1, p2[1][1] * vs1));
+          vs0[gi] = va.get(gi);
+          vs1[gi] = vc.get(gi);
+          vmax = fmaxf(vmax, fmaxf(vs0[gi], vs1[gi]));
+        }
+        const uint32_t vbits = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
+        if (vbits != 0u) {
+          const int e = static_cast<int>((vbits >> 23) & 0xFFu) - 127 + vexp;
+          if (e < -6 || e > 6) {  // warp-uniform
+            const int nexp = max(-120, min(120, vexp - e));
+            const float r = __int_as_float((127 + max(-126, min(127, nexp - vexp))) << 23);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) o_acc[c][j][k] *= r;
+#pragma unroll
+            for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+              for (int k = 0; k < 4; ++k) sp_acc[gi][k] *= r;
+            vexp = nexp;
+          }
+        }
+        const float vf = __int_as_float((127 + vexp) << 23);
+        const float q00 = p2[0][0] * vf, q01 = p2[0][1] * vf;
+        const float q10 = p2[1][0] * vf, q11 = p2[1][1] * vf;
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          pb[gi][0] = movmatrix_trans(pack_f16x2(q00 * vs0[gi], q01 * vs0[gi]));
+          pb[gi][1] = movmatrix_trans(pack_f16x2(q10 * vs1[gi], q11 * vs1[gi]));
         }
       }
       const uint32_t mask_a = g < 4 ? 0xFFFFFFFFu : 0u;
@@ -1285,17 +1330,18 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
             const int c = 2 * cp + e;
             const int gi = c / CPG;
             const uint32_t b0 = pb[gi][0] & msk, b1 = pb[gi][1] & msk;
+            // rows g: even dims (1024 + code), rows g + 8: odd dims (1024 + 16 code)
             const uint32_t wab = wr[2 * e], wcd = wr[2 * e + 1];
-            const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
-            const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
-            mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, b0, b1);
-            mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, b0, b1);
+            const uint32_t yab = wab >> 8, ycd = wcd >> 8;
+            mma_f16_16816(o_acc[c][0], h_lo(wab), h_hi(wab), h_lo(wcd), h_hi(wcd), b0, b1);
+            mma_f16_16816(o_acc[c][1], h_lo(yab), h_hi(yab), h_lo(ycd), h_hi(ycd), b0, b1);
           }
         }
       }
+      const uint32_t ones16 = 0x3C003C00u;  // f16x2 (1, 1)
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi)
-        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
+        mma_f16_16816(sp_acc[gi], ones16, ones16, ones16, ones16, pb[gi][0], pb[gi][1]);
     } else {
     // ---------------- scores S^T[token][col] for two m16 sub-tiles -------
     // Per scale group: partial dot products on the tensor cores (the first
