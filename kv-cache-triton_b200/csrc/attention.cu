@@ -230,19 +230,22 @@ struct FastParams {
 };
 
 // Quantize one d-wide row with a warp: lane l owns dims [DPL*l, DPL*l + DPL)
-// and returns their packed nibbles (low nibble = even dim) and its group's
-// fp32 scale.  Same arithmetic as quantize_kernel for each tie mode.
+// (v, loaded by load_row_lane) and returns their packed nibbles (low nibble =
+// even dim) and its group's fp32 scale.  Same arithmetic as quantize_kernel
+// for each tie mode.
+template <int D>
+__device__ __forceinline__ void load_row_lane(const void *x, int dt, int64_t off, int lane,
+                                              float (&v)[D / 32]) {
+#pragma unroll
+  for (int e = 0; e < D / 32; ++e) v[e] = load_as_f32(x, dt, off + (D / 32) * lane + e);
+}
 template <int D, int G>
-__device__ __forceinline__ void quant_row_warp(const void *x, int dt, int64_t off, int tie,
-                                               int lane, uint32_t &w, float &scale) {
+__device__ __forceinline__ void quant_row_regs(const float (&v)[D / 32], int tie, uint32_t &w,
+                                               float &scale) {
   constexpr int DPL = D / 32, LPG = G / DPL;
-  float v[DPL];
   float mx = 0.0f;
 #pragma unroll
-  for (int e = 0; e < DPL; ++e) {
-    v[e] = load_as_f32(x, dt, off + DPL * lane + e);
-    mx = fmaxf(mx, fabsf(v[e]));
-  }
+  for (int e = 0; e < DPL; ++e) mx = fmaxf(mx, fabsf(v[e]));
 #pragma unroll
   for (int o = 1; o < LPG; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   w = 0;
@@ -609,47 +612,20 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     for (int i = 0; i < pre; ++i) issue(i);
   }
 
-  // ---- fused append: the owner warp of the new row quantizes it once ----
-  // into app_buf (and, for hc == 0, into the cache in HBM); the same warp
-  // copies it over the staged row once that tile has landed.
+  // ---- fused append: the owner warp of the new row loads it now (the loads
+  // complete while the tiles stream) and quantizes it when it reaches the
+  // row's tile: into the staged copy and, for hc == 0, into the cache in HBM.
   constexpr int DPL = D / 32, NBL = DPL / 2;  // dims / packed bytes per lane
   int app_key = -1;                           // (local tile) * NWARP + owner warp
+  float app_k[DPL], app_v[DPL];
   {
     const int app_tile = P.app_row >= 0 ? P.app_row / TOK : -1;
     if (app_tile >= t_begin && app_tile < t_end) {
       const int app_warp = (P.app_row - app_tile * TOK) / WROWS;
       app_key = (app_tile - t_begin) * NWARP + app_warp;
       if (warp == app_warp) {
-        uint32_t kw, vw;
-        float ksf, vsf;
-        quant_row_warp<D, G>(P.kn, P.kn_dtype, u_b * P.kn_sb + u_kvh * P.kn_sh, P.app_tie, lane,
-                             kw, ksf);
-        quant_row_warp<D, G>(P.vn, P.kn_dtype, u_b * P.vn_sb + u_kvh * P.vn_sh, P.app_tie, lane,
-                             vw, vsf);
-        const ST kst = from_f32<ST>(ksf), vst = from_f32<ST>(vsf);
-        const uint32_t ab = smem_u32(app_buf);
-        st_bytes_shared<NBL>(ab + NBL * lane, kw);
-        st_bytes_shared<NBL>(ab + Cfg::P + NBL * lane, vw);
-        const bool lead = (DPL * lane) % G == 0;
-        const int so = (DPL * lane / G) * static_cast<int>(sizeof(ST));
-        if (lead) {
-          st_scale_shared<ST>(ab + 2 * Cfg::P + so, kst);
-          st_scale_shared<ST>(ab + 2 * Cfg::P + Cfg::SROW + so, vst);
-        }
-        if (u_hc == 0) {  // one writer per (b, kvh) row
-          const int64_t r = P.app_row;
-          st_bytes_global<NBL>(P.kpw + u_b * P.kp_sb + u_kvh * P.kp_sh + r * P.kp_st + NBL * lane,
-                               kw);
-          st_bytes_global<NBL>(P.vpw + u_b * P.vp_sb + u_kvh * P.vp_sh + r * P.vp_st + NBL * lane,
-                               vw);
-          if (lead) {
-            *reinterpret_cast<ST *>(const_cast<char *>(P.ks) + u_b * P.ks_sb + u_kvh * P.ks_sh +
-                                    r * Cfg::SROW + so) = kst;
-            *reinterpret_cast<ST *>(const_cast<char *>(P.vs) + u_b * P.vs_sb + u_kvh * P.vs_sh +
-                                    r * Cfg::SROW + so) = vst;
-          }
-        }
-        __syncwarp();
+        load_row_lane<D>(P.kn, P.kn_dtype, u_b * P.kn_sb + u_kvh * P.kn_sh, lane, app_k);
+        load_row_lane<D>(P.vn, P.kn_dtype, u_b * P.vn_sb + u_kvh * P.vn_sh, lane, app_v);
       }
     }
   }
@@ -1133,17 +1109,34 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     const int tok0 = ti * TOK + WROWS * warp;  // first token row of this warp
     if (i * NWARP + warp == app_key) {
       // the staged copy of the new row came from HBM before (or while) it was
-      // written: overwrite it with this warp's own quantization
+      // written: quantize the row and overwrite the staged copy (and, once
+      // per (b, kvh), write it to the cache)
+      uint32_t kw, vw;
+      float ksf, vsf;
+      quant_row_regs<D, G>(app_k, P.app_tie, kw, ksf);
+      quant_row_regs<D, G>(app_v, P.app_tie, vw, vsf);
+      const ST kst = from_f32<ST>(ksf), vst = from_f32<ST>(vsf);
       const int r = P.app_row - ti * TOK;
       const int o = NBL * lane;
       const uint32_t off = r * P_ + 16 * ((o >> 4) ^ ((r >> Cfg::SH) & Cfg::SWZ)) + (o & 15);
-      const uint32_t ab = smem_u32(app_buf);
-      st_bytes_shared<NBL>(kp + off, ld_bytes_shared<NBL>(ab + o));
-      st_bytes_shared<NBL>(vp + off, ld_bytes_shared<NBL>(ab + Cfg::P + o));
-      if (lane < Cfg::SROW / 2) {  // scale rows, 2 bytes per lane
-        const uint32_t so = r * Cfg::SROW + 2 * lane;
-        st_bytes_shared<2>(ksb + so, ld_bytes_shared<2>(ab + 2 * Cfg::P + 2 * lane));
-        st_bytes_shared<2>(vsb + so, ld_bytes_shared<2>(ab + 2 * Cfg::P + Cfg::SROW + 2 * lane));
+      st_bytes_shared<NBL>(kp + off, kw);
+      st_bytes_shared<NBL>(vp + off, vw);
+      const bool lead = (DPL * lane) % G == 0;
+      const int so = (DPL * lane / G) * static_cast<int>(sizeof(ST));
+      if (lead) {
+        st_scale_shared<ST>(ksb + r * Cfg::SROW + so, kst);
+        st_scale_shared<ST>(vsb + r * Cfg::SROW + so, vst);
+      }
+      if (u_hc == 0) {  // one writer per (b, kvh) row
+        const int64_t rr = P.app_row;
+        st_bytes_global<NBL>(P.kpw + u_b * P.kp_sb + u_kvh * P.kp_sh + rr * P.kp_st + o, kw);
+        st_bytes_global<NBL>(P.vpw + u_b * P.vp_sb + u_kvh * P.vp_sh + rr * P.vp_st + o, vw);
+        if (lead) {
+          *reinterpret_cast<ST *>(const_cast<char *>(P.ks) + u_b * P.ks_sb + u_kvh * P.ks_sh +
+                                  rr * Cfg::SROW + so) = kst;
+          *reinterpret_cast<ST *>(const_cast<char *>(P.vs) + u_b * P.vs_sb + u_kvh * P.vs_sh +
+                                  rr * Cfg::SROW + so) = vst;
+        }
       }
       // order these generic writes before the TMA refill of the stage
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
