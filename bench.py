@@ -2,22 +2,26 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (per rank): Llama-3.1-8B single-layer decode, B=16, 32 q heads,
-8 KV heads, d=128, context S=4096, INT4 group size 32, bf16 q/K/V, K
-channels scaled by log-uniform [0.5, 8] factors, seeded synthetic data.  A
-step = quantize-append of the new K/V token + fused decode attention over
-the S-token INT4 cache, for one layer, in ONE launch (kv4_append_attention:
-the attention kernel quantizes the new row itself).  The timed loop replays a
-CUDA graph holding one step per layer (a model's per-token decode graph).  Steps rotate over 32
-layer caches (2.4 GB resident per GPU), so every step reads its cache from
-HBM, not L2 (126 MB).
+Workload: Llama-3.1-8B single-layer decode, B=16, 32 q heads, 8 KV heads,
+d=128, context S=4096, INT4 group size 32, bf16 q/K/V, K channels scaled by
+log-uniform [0.5, 8] factors, seeded synthetic data.  A step = quantize-append
+of the new K/V token + fused decode attention over the S-token INT4 cache,
+for one layer, in ONE launch (kv4_append_attention: the attention kernel
+quantizes the new row itself).  The timed loop replays a CUDA graph holding
+one step per layer (a model's per-token decode graph).  Steps rotate over
+layer caches of >= 2.4 GB in total, so every step reads its cache from HBM,
+not L2 (126 MB).
 
-`value` = algorithmic bytes of all ranks' steps / max-over-ranks device time
-(GB/s).  `e2e` = the same metric through the public Python API with pinned
-host q/k/v copied in and the output copied out every step.  With N > 1 each
-rank owns its own batch shard (weak scaling, no collective on the data path).
-`--impl reference` times the reference's CPU formulation (oracle/torch_ref.py)
-on the host cores on a bounded batch sample.
+With N ranks the KV heads of the one problem are split over the ranks
+(rank r owns KV heads [r*Hkv/N, (r+1)*Hkv/N) and their q heads): strong
+scaling, no collective on the data path.  `value` = algorithmic bytes of the
+whole problem per step / max-over-ranks device time (GB/s).  `e2e` = the same
+metric through the public Python API with pinned host q/k/v copied in and the
+output copied out every step.  Rank 0 at N=1 also reports the other
+workloads (batch-1 long context, the 70B one-KV-head-per-GPU shape) and the
+reference's microbenchmark sweeps (B=1, S=512..32K; G=32/64/128) next to the
+reference's own Triton kernel.  `--impl reference` times the reference's CPU
+formulation (oracle/torch_ref.py) on the host cores.
 """
 
 from __future__ import annotations
@@ -43,35 +47,49 @@ WORKLOADS = {
     "long16k": dict(B=1, HQ=32, HKV=8, S=16384),
     "long64k": dict(B=1, HQ=32, HKV=8, S=65536),
     "long128k": dict(B=1, HQ=32, HKV=8, S=131072),
-    # config 4: Llama-3.1-70B shape with one KV head (and its 8 q heads) per GPU
-    "config4": dict(B=32, HQ=8, HKV=1, S=16384),
+    # Llama-3.1-70B decode layer (8 GPUs: one KV head and its 8 q heads each)
+    "config4": dict(B=32, HQ=64, HKV=8, S=16384),
 }
 B, HQ, HKV, S, D, G = 16, 32, 8, 4096, 128, 32
 LAYERS = 32
 METRIC = "INT4-KV decode attention HBM GB/s (Llama-3.1-8B shape, B16, S4096, G32)"
 
 
-def attn_bytes(ss=2, qs=2):
+HQ_L, HKV_L = HQ, HKV  # this rank's share of the heads (KV-head sharding)
+
+
+def attn_bytes(ss=2, qs=2, hq=None, hkv=None):
     """Algorithmic bytes of one decode-attention launch: packed K/V + scales
-    over the S-token cache, q read, output written."""
-    return 2 * B * HKV * S * (D // 2 + (D // G) * ss) + 2 * B * HQ * D * qs
+    over the S-token cache, q read, output written (whole problem unless
+    hq/hkv name a share)."""
+    hq = HQ if hq is None else hq
+    hkv = HKV if hkv is None else hkv
+    return 2 * B * hkv * S * (D // 2 + (D // G) * ss) + 2 * B * hq * D * qs
 
 
-def append_bytes(ss=2, xs=2):
-    return 2 * B * HKV * (D * xs + D // 2 + (D // G) * ss)
+def append_bytes(ss=2, xs=2, hkv=None):
+    hkv = HKV if hkv is None else hkv
+    return 2 * B * hkv * (D * xs + D // 2 + (D // G) * ss)
 
 
-def step_bytes():
-    return attn_bytes() + append_bytes()
+def step_bytes(hq=None, hkv=None):
+    return attn_bytes(hq=hq, hkv=hkv) + append_bytes(hkv=hkv)
 
 
-def set_workload(name):
-    global B, HQ, HKV, S, LAYERS, METRIC
+def local_step_bytes():
+    return step_bytes(HQ_L, HKV_L)
+
+
+def set_workload(name, ws=1):
+    global B, HQ, HKV, S, LAYERS, METRIC, HQ_L, HKV_L
     w = WORKLOADS[name]
     B, HQ, HKV, S = w["B"], w["HQ"], w["HKV"], w["S"]
-    # enough layer caches to keep ~2.4 GB resident (>> the 126 MB L2)
-    LAYERS = max(2, min(32, -(-2_400_000_000 // attn_bytes())))
-    shape = "Llama-3.1-70B shape, 1 KV head/GPU" if name == "config4" else "Llama-3.1-8B shape"
+    if HKV % ws:
+        raise SystemExit(f"{HKV} KV heads do not split over {ws} ranks")
+    HQ_L, HKV_L = HQ // ws, HKV // ws
+    # enough layer caches to keep ~2.4 GB resident per GPU (>> the 126 MB L2)
+    LAYERS = max(2, min(32, -(-2_400_000_000 // attn_bytes(hq=HQ_L, hkv=HKV_L))))
+    shape = "Llama-3.1-70B shape" if name == "config4" else "Llama-3.1-8B shape"
     METRIC = f"INT4-KV decode attention HBM GB/s ({shape}, B{B}, S{S}, G{G})"
 
 
@@ -82,9 +100,9 @@ def workload_config(args, ws):
                         "+ INT4 decode attention",
             "batch": B, "q_heads": HQ, "kv_heads": HKV, "seq_len": S, "d_head": D,
             "group_size": G,
-            "parallelism": f"batch shard x{ws} (no collective)" if ws > 1 else "single",
-            "l2": f"inputs larger than L2: steps rotate over {LAYERS} layer caches "
-                  f"({LAYERS * attn_bytes() / 1e9:.2f} GB)",
+            "parallelism": (f"kv-head shard x{ws}: {HKV // ws} KV heads and {HQ // ws} q heads "
+                            "per rank, no collective") if ws > 1 else "single",
+            "l2": "inputs larger than L2: steps rotate over layer caches of >= 2.4 GB per GPU",
             "bytes_per_step": step_bytes()}
 
 
@@ -154,20 +172,34 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def build_caches(dev, seed=0):
+def build_caches(dev, seed=0, hq=None, hkv=None, layers=None):
+    """Layer caches of this rank's heads (full-length INT4 K/V) plus q and the
+    new token's K/V per layer."""
     from kvint4.cache import Int4KVStore
+    hq = HQ_L if hq is None else hq
+    hkv = HKV_L if hkv is None else hkv
+    layers = LAYERS if layers is None else layers
     g = torch.Generator(device=dev).manual_seed(seed)
     store = Int4KVStore(G, capacity=S)
     fac = torch.exp(torch.empty(D, device=dev).uniform_(math.log(0.5), math.log(8.0),
                                                         generator=g))
-    for layer in range(LAYERS):
-        k = (torch.randn(B, HKV, S, D, device=dev, generator=g) * fac).to(torch.bfloat16)
-        v = torch.randn(B, HKV, S, D, device=dev, generator=g).to(torch.bfloat16)
-        store.append(k, v, layer)
-        del k, v
-    q = torch.randn(LAYERS, B, HQ, 1, D, device=dev, generator=g).to(torch.bfloat16)
-    kn = (torch.randn(LAYERS, B, HKV, 1, D, device=dev, generator=g) * fac).to(torch.bfloat16)
-    vn = torch.randn(LAYERS, B, HKV, 1, D, device=dev, generator=g).to(torch.bfloat16)
+    for layer in range(layers):
+        for b0 in range(0, B, 8):  # in batch chunks: bounded bf16 staging
+            b1 = min(B, b0 + 8)
+            k = (torch.randn(b1 - b0, hkv, S, D, device=dev, generator=g) * fac).to(torch.bfloat16)
+            v = torch.randn(b1 - b0, hkv, S, D, device=dev, generator=g).to(torch.bfloat16)
+            if b0 == 0:
+                store.append(torch.empty(B, hkv, 0, D, device=dev, dtype=torch.bfloat16),
+                             torch.empty(B, hkv, 0, D, device=dev, dtype=torch.bfloat16), layer)
+            st = store.layer(layer)
+            from kvint4 import ops
+            ops.append_kv(k, v, st.k_packed_buf[b0:b1], st.k_scales_buf[b0:b1],
+                          st.v_packed_buf[b0:b1], st.v_scales_buf[b0:b1], 0, G)
+            del k, v
+        store.layer(layer).seq_len = S
+    q = torch.randn(layers, B, hq, 1, D, device=dev, generator=g).to(torch.bfloat16)
+    kn = (torch.randn(layers, B, hkv, 1, D, device=dev, generator=g) * fac).to(torch.bfloat16)
+    vn = torch.randn(layers, B, hkv, 1, D, device=dev, generator=g).to(torch.bfloat16)
     return store, q, kn, vn
 
 
@@ -179,7 +211,7 @@ def run_ours(args, ws, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     store, q, kn, vn = build_caches(dev, seed=rank)
-    out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B, HQ_L, 1, D, dtype=torch.bfloat16, device=dev)
     st = torch.cuda.current_stream(dev)
 
     def append_op(l):
@@ -257,9 +289,9 @@ def run_ours(args, ws, rank, local):
 
     # ---- e2e: public API, pinned host buffers in and out every step ----
     # each step's q, k, v packed in one pinned host row: one copy in per step
-    nq, nk = B * HQ * D, B * HKV * D
+    nq, nk = B * HQ_L * D, B * HKV_L * D
     hin = torch.randn(args.steps, nq + 2 * nk).to(torch.bfloat16).pin_memory()
-    hout = torch.empty(args.steps, B, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
+    hout = torch.empty(args.steps, B, HQ_L, 1, D, dtype=torch.bfloat16).pin_memory()
     from models.llama3.kv_cache import QuantizedKVCache
     caches = []
     for l in range(LAYERS):
@@ -267,16 +299,16 @@ def run_ours(args, ws, rank, local):
         c._store._layers[0] = store.layer(l)
         caches.append(c)
     din = torch.empty(nq + 2 * nk, dtype=torch.bfloat16, device=dev)
-    dq = din[:nq].view(B, HQ, 1, D)
-    dk = din[nq:nq + nk].view(B, HKV, 1, D)
-    dv = din[nq + nk:].view(B, HKV, 1, D)
-    do = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+    dq = din[:nq].view(B, HQ_L, 1, D)
+    dk = din[nq:nq + nk].view(B, HKV_L, 1, D)
+    dv = din[nq + nk:].view(B, HKV_L, 1, D)
+    do = torch.empty(B, HQ_L, 1, D, dtype=torch.bfloat16, device=dev)
 
     def e2e_step(i):
         c = caches[i % LAYERS]
         c._store.layer(0).seq_len = S - 1
         din.copy_(hin[i % args.steps], non_blocking=True)
-        o = c.append_attend(dq, dk, dv, 0, do, n_q_heads=HQ, n_kv_heads=HKV)
+        o = c.append_attend(dq, dk, dv, 0, do, n_q_heads=HQ_L, n_kv_heads=HKV_L)
         hout[i % args.steps].copy_(o, non_blocking=True)
 
     for i in range(args.warmup):
@@ -306,10 +338,10 @@ def run_ours(args, ws, rank, local):
         return None
     peak, peak_kind = _peaks()
     per_step_ms = ms / args.steps
-    value = ws * step_bytes() * args.steps / (ms * 1e-3) / 1e9
-    achieved = step_bytes() / (attn_avg_ms * 1e-3) / 1e9
-    h2d = (B * HQ * D + 2 * B * HKV * D) * 2
-    d2h = B * HQ * D * 2
+    value = step_bytes() * args.steps / (ms * 1e-3) / 1e9  # whole problem / max-rank time
+    achieved = local_step_bytes() / (attn_avg_ms * 1e-3) / 1e9  # per GPU
+    h2d = (B * HQ_L * D + 2 * B * HKV_L * D) * 2
+    d2h = B * HQ_L * D * 2
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -320,13 +352,13 @@ def run_ours(args, ws, rank, local):
         "ms_per_step": round(per_step_ms, 5),
         "us_per_step": round(per_step_ms * 1e3, 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16 q/out, int4 KV codes, bf16 scales, fp32 accumulate",
         "data": "synthetic (seeded N(0,1), K channels x log-uniform[0.5,8])",
         "config": workload_config(args, ws),
         "gpu_launches": args.steps * int(p.kernels),
-        "e2e": {"value": round(ws * step_bytes() * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
+        "e2e": {"value": round(step_bytes() * args.steps / (e2e_ms * 1e-3) / 1e9, 1),
                 "unit": "GB/s", "us_per_step": round(e2e_ms * 1e3 / args.steps, 2),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "kernel": "kv4_attn_fast",
@@ -342,9 +374,124 @@ def run_ours(args, ws, rank, local):
     }
     if gpu_ref is not None:
         line["gpu_reference"] = gpu_ref
+    if ws == 1 and not args.no_extra:
+        line["workloads"] = extra_workloads(dev, with_reference=not args.no_gpu_reference)
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     return line
+
+
+class workload_dims:
+    """Temporarily switch the module's problem dimensions (extra workloads)."""
+
+    def __init__(self, **kw):
+        self.kw = kw
+
+    def __enter__(self):
+        g = globals()
+        self.saved = {k: g[k] for k in ("B", "HQ", "HKV", "S", "G", "HQ_L", "HKV_L", "LAYERS")}
+        g.update(self.kw)
+        g["HQ_L"], g["HKV_L"] = g["HQ"], g["HKV"]
+        if "LAYERS" not in self.kw:
+            g["LAYERS"] = max(2, min(32, -(-2_400_000_000 // attn_bytes())))
+        return self
+
+    def __exit__(self, *a):
+        globals().update(self.saved)
+
+
+def _graph_time_us(step, span, reps, st):
+    """Device time per step of `reps` replays of a graph of `span` steps."""
+    for l in range(span):
+        step(l)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for l in range(span):
+            step(l)
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(reps):
+        graph.replay()
+    t1.record(st)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) * 1e3 / (span * reps)
+
+
+def extra_workloads(dev, with_reference=True):
+    """The other workloads (fused append + attention steps, one graph per
+    token over >= 2.4 GB of layer caches) and the reference's microbenchmark
+    sweeps (attention alone, B=1, 32/8 heads, d=128) beside the reference's
+    own Triton kernel on the same caches."""
+    from kvint4 import ops
+    peak, _ = _peaks()
+    st = torch.cuda.current_stream(dev)
+    ref_fn = None
+    if with_reference:
+        try:
+            from oracle import triton_ref
+            ref_fn = triton_ref.llama3_attention().attention_forward_quant_gqa
+        except Exception:
+            ref_fn = None
+    res = {}
+    for name, dims in (("long16k", dict(B=1, HQ=32, HKV=8, S=16384)),
+                       ("long64k", dict(B=1, HQ=32, HKV=8, S=65536)),
+                       ("long128k", dict(B=1, HQ=32, HKV=8, S=131072)),
+                       ("llama70b_one_kv_head_per_gpu", dict(B=32, HQ=8, HKV=1, S=16384))):
+        with workload_dims(**dims):
+            store, q, kn, vn = build_caches(dev)
+            out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+
+            def step(l):
+                kp, ks, vp, vs = store.layer(l).views()
+                ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False)
+
+            with ClockSampler(dev.index or 0) as clk:
+                us = _graph_time_us(step, LAYERS, max(2, 64 // LAYERS), st)
+            gbs = step_bytes() / (us * 1e-6) / 1e9
+            res[name] = {"B": B, "q_heads": HQ, "kv_heads": HKV, "seq_len": S, "group_size": G,
+                         "us_per_step": round(us, 2), "GB/s": round(gbs, 1),
+                         "frac": round(gbs / peak, 4), "layers": LAYERS,
+                         "clocks": clk.summary()}
+            del store, q, kn, vn
+            torch.cuda.empty_cache()
+    sweeps = []
+    points = [(s_, 32) for s_ in (512, 1024, 2048, 4096, 8192, 16384, 32768)]
+    points += [(4096, 64), (4096, 128)]
+    for s_, g_ in points:
+        with workload_dims(B=1, HQ=32, HKV=8, S=s_, G=g_, LAYERS=None):
+            globals()["LAYERS"] = max(2, min(64, -(-256_000_000 // attn_bytes())))
+            store, q, _, _ = build_caches(dev)
+            out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+
+            def attn(l):
+                kp, ks, vp, vs = store.layer(l).views()
+                ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
+
+            us = _graph_time_us(attn, LAYERS, max(2, 128 // LAYERS), st)
+            row = {"seq_len": S, "group_size": G, "layer_copies": LAYERS,
+                   "l2_resident": LAYERS * attn_bytes() < 126e6,
+                   "ours_us": round(us, 2),
+                   "ours_GB/s": round(attn_bytes() / (us * 1e-6) / 1e9, 1)}
+            if ref_fn is not None:
+                try:
+                    def ref(l):
+                        kp, ks, vp, vs = store.layer(l).views()
+                        ref_fn(q[l], kp, ks, vp, vs, n_q_heads=HQ, n_kv_heads=HKV, group_size=G)
+
+                    rus = _graph_time_us(ref, LAYERS, max(2, 32 // LAYERS), st)
+                    row["reference_triton_us"] = round(rus, 2)
+                    row["speedup_vs_reference"] = round(rus / us, 1)
+                except Exception as e:  # noqa: BLE001
+                    row["reference_triton"] = f"unavailable: {type(e).__name__}"
+            sweeps.append(row)
+            del store, q
+            torch.cuda.empty_cache()
+    res["sweep_b1_32q_8kv_d128"] = sweeps
+    return res
 
 
 def triton_reference_leg(store, q, span, reps, warmup, st):
@@ -452,7 +599,7 @@ def run_reference(args, ws, rank):
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 3), "us_per_step": round(step_s * 1e6, 1),
-        "higher_is_better": True, "scaling": "weak",
+        "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "impl": "reference",
         "config": workload_config(args, ws),
@@ -577,6 +724,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other workloads and the sweeps (rank 0, N=1)")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip timing the reference's Triton kernel on the same caches")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -586,9 +735,9 @@ def main():
                     help="config2 = 8B decode at batch 16 (the headline); long* = batch-1 long context; "
                          "config4 = 70B shape, one KV head per GPU")
     args = ap.parse_args()
-    set_workload(args.workload)
     args.warmup = max(args.warmup, 3)
     ws, rank, local = _dist()
+    set_workload(args.workload, 1 if (args.impl == "reference" or args.shard == "seq") else ws)
     if args.impl == "reference":
         line = run_reference(args, ws, rank)
     else:
