@@ -637,7 +637,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
   float sp_acc[NG][4];                  // sum of P' per group (for the +128 bias of V codes)
   float m_run[2], l_run[2];
   float col_inv[2];  // score factor of columns 2tg, 2tg+1 (log2 domain)
-  int vexp = 0;      // PAIR: per-warp power-of-two factor of the f16 P'' (see below)
+  int vexp = 0;      // MODE 0/2: per-warp power-of-two factor of the f16 P'' (adjust_vexp)
   int col_lim[2];
   int lim_min = 0;  // smallest key limit over the CTA's columns (warp-uniform)
 
@@ -879,7 +879,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
         const int d0 = 32 * c + 4 * g + 2 * j;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {  // column 2tg + cc
-          if constexpr (PAIR) {
+          if constexpr (!SPLIT) {
             // f16 V operands: even dims hold 1024 + code, odd dims 1024 + 16 code;
             // undo the warp's 2^vexp factor
             const float sp = sp_acc[gi][cc];
@@ -1089,6 +1089,33 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
   }
   const uint32_t s_row0 = (WROWS * warp + g) * Cfg::SROW;        // scale row of token row g
 
+  // f16 V operands (MODE 0 and 2): keep the step's largest V scale times
+  // 2^vexp within [2^-6, 2^6] (P <= 2^8, so P * v_scale * 2^vexp stays in
+  // the f16 range with full precision); when it leaves that range, move
+  // vexp and rescale the accumulators exactly.  Returns 2^vexp.
+  auto adjust_vexp = [&](float vmax) -> float {
+    const uint32_t vbits = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
+    if (vbits != 0u) {
+      const int e = static_cast<int>((vbits >> 23) & 0xFFu) - 127 + vexp;
+      if (e < -6 || e > 6) {  // warp-uniform
+        const int nexp = max(-120, min(120, vexp - e));
+        const float r = __int_as_float((127 + max(-126, min(127, nexp - vexp))) << 23);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o_acc[c][j][k] *= r;
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sp_acc[gi][k] *= r;
+        vexp = nexp;
+      }
+    }
+    return __int_as_float((127 + vexp) << 23);
+  };
+
   load_unit();  // q loads overlap the first TMA loads already in flight
   __syncwarp();  // the bias quads written by lanes g == 0 are read by the whole warp
   int stage = -1;
@@ -1282,26 +1309,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
           vs1[gi] = vc.get(gi);
           vmax = fmaxf(vmax, fmaxf(vs0[gi], vs1[gi]));
         }
-        const uint32_t vbits = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
-        if (vbits != 0u) {
-          const int e = static_cast<int>((vbits >> 23) & 0xFFu) - 127 + vexp;
-          if (e < -6 || e > 6) {  // warp-uniform
-            const int nexp = max(-120, min(120, vexp - e));
-            const float r = __int_as_float((127 + max(-126, min(127, nexp - vexp))) << 23);
-#pragma unroll
-            for (int c = 0; c < NCH; ++c)
-#pragma unroll
-              for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) o_acc[c][j][k] *= r;
-#pragma unroll
-            for (int gi = 0; gi < NG; ++gi)
-#pragma unroll
-              for (int k = 0; k < 4; ++k) sp_acc[gi][k] *= r;
-            vexp = nexp;
-          }
-        }
-        const float vf = __int_as_float((127 + vexp) << 23);
+        const float vf = adjust_vexp(vmax);
         const float q00 = p2[0][0] * vf, q01 = p2[0][1] * vf;
         const float q10 = p2[1][0] * vf, q11 = p2[1][1] * vf;
 #pragma unroll
@@ -1478,6 +1486,21 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
         }
 
     // ---------------- per sub-tile: P' = P * v_scale, then O^T += V^T P' -
+    // (MODE 0: V codes as f16 operands, P'' = P * v_scale * 2^vexp)
+    [[maybe_unused]] SRow<NG, ST> vrow[2][2];
+    [[maybe_unused]] float vfac = 1.0f;
+    if constexpr (!SPLIT) {
+      float vmax = 0.0f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          vrow[h][r].load(vsb + s_row0 + (16 * h + 8 * r) * Cfg::SROW);
+#pragma unroll
+          for (int gi = 0; gi < NG; ++gi) vmax = fmaxf(vmax, vrow[h][r].get(gi));
+        }
+      vfac = adjust_vexp(vmax);
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t pb[NG][2];
@@ -1500,16 +1523,15 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
           pbl[gi][1] = movmatrix_trans(l1);
         }
       } else {
-        // P' = P * v_scale in fp32 (one rounding to bf16), the scale rows of
-        // tokens g and g+8 loaded once each, then transposed into the B layout
-        SRow<NG, ST> ra, rc;
-        ra.load(vsb + s_row0 + (16 * h) * Cfg::SROW);
-        rc.load(vsb + s_row0 + (16 * h + 8) * Cfg::SROW);
+        // P'' = P * v_scale * 2^vexp in fp32, one rounding to f16, then
+        // transposed into the B layout
+        const float q00 = p[h][0][0] * vfac, q01 = p[h][0][1] * vfac;
+        const float q10 = p[h][1][0] * vfac, q11 = p[h][1][1] * vfac;
 #pragma unroll
         for (int gi = 0; gi < NG; ++gi) {
-          const float vs0 = ra.get(gi), vs1 = rc.get(gi);
-          pb[gi][0] = movmatrix_trans(pack_bf16x2(p[h][0][0] * vs0, p[h][0][1] * vs0));
-          pb[gi][1] = movmatrix_trans(pack_bf16x2(p[h][1][0] * vs1, p[h][1][1] * vs1));
+          const float vs0 = vrow[h][0].get(gi), vs1 = vrow[h][1].get(gi);
+          pb[gi][0] = movmatrix_trans(pack_f16x2(q00 * vs0, q01 * vs0));
+          pb[gi][1] = movmatrix_trans(pack_f16x2(q10 * vs1, q11 * vs1));
         }
       }
 #pragma unroll
@@ -1523,21 +1545,31 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
           const int c = 2 * cp + e;
           const int gi = c / CPG;
           const uint32_t wab = wr[2 * e], wcd = wr[2 * e + 1];
-          const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
-          const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
-          mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pb[gi][0], pb[gi][1]);
-          mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pb[gi][0], pb[gi][1]);
           if constexpr (SPLIT) {
+            const uint32_t v0 = nib_lo0(wab), v1 = nib_hi0(wab), v2 = nib_lo0(wcd), v3 = nib_hi0(wcd);
+            const uint32_t v4 = nib_lo1(wab), v5 = nib_hi1(wab), v6 = nib_lo1(wcd), v7 = nib_hi1(wcd);
+            mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pb[gi][0], pb[gi][1]);
+            mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pb[gi][0], pb[gi][1]);
             mma_bf16_16816(o_acc[c][0], v0, v1, v2, v3, pbl[gi][0], pbl[gi][1]);
             mma_bf16_16816(o_acc[c][1], v4, v5, v6, v7, pbl[gi][0], pbl[gi][1]);
+          } else {
+            const uint32_t yab = wab >> 8, ycd = wcd >> 8;
+            mma_f16_16816(o_acc[c][0], h_lo(wab), h_hi(wab), h_lo(wcd), h_hi(wcd), pb[gi][0],
+                          pb[gi][1]);
+            mma_f16_16816(o_acc[c][1], h_lo(yab), h_hi(yab), h_lo(ycd), h_hi(ycd), pb[gi][0],
+                          pb[gi][1]);
           }
         }
       }
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
-        if constexpr (SPLIT)
+        if constexpr (SPLIT) {
+          mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pb[gi][0], pb[gi][1]);
           mma_bf16_16816(sp_acc[gi], ones, ones, ones, ones, pbl[gi][0], pbl[gi][1]);
+        } else {
+          constexpr uint32_t ones16 = 0x3C003C00u;  // f16x2 (1, 1)
+          mma_f16_16816(sp_acc[gi], ones16, ones16, ones16, ones16, pb[gi][0], pb[gi][1]);
+        }
       }
     }
 
