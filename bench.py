@@ -639,22 +639,27 @@ def run_seq_shard(args, ws, rank, local):
     out = torch.empty(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
     st = torch.cuda.current_stream(dev)
 
+    # ranks exchange partials over peer memory (kv4_lse_exchange): two
+    # launches per step, no collective library, so the step sits in a graph
+    xchg = (shard.PeerExchange(rows=B * HQ, d=D, device=dev)
+            if ws > 1 and args.seq_transport == "peer" else None)
+
     def step(l):
         kp, ks, vp, vs = store.layer(l).views()
         if ws == 1:
             ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
         else:
             shard.seq_sharded_attention(q[l], kp, ks, vp, vs, k_offset=lo, sk_total=S,
-                                        group_size=G, out=out)
+                                        group_size=G, out=out, exchange=xchg)
 
     for l in range(layers):
         step(l)
     torch.cuda.synchronize()
-    # Eager launches: the collectives are not captured in a CUDA graph (a
-    # capture that fails on one rank only would leave the ranks' collective
-    # sequences mismatched).  With one GPU the step is a plain attention call.
+    # NCCL all-gathers run eagerly (a capture that failed on one rank only
+    # would leave the ranks' collective sequences mismatched); the peer
+    # exchange and the single-GPU step replay from a CUDA graph.
     graph = None
-    if ws == 1:
+    if ws == 1 or xchg is not None:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             for l in range(layers):
@@ -705,15 +710,16 @@ def run_seq_shard(args, ws, rank, local):
         "config": {"workload": f"{args.workload}: batch-1 decode attention, sequence sharded",
                    "batch": B, "q_heads": HQ, "kv_heads": HKV, "seq_len": S, "d_head": D,
                    "group_size": G, "tokens_per_rank": n,
-                   "parallelism": f"sequence shard x{ws}: partial attention + NCCL all-gather "
-                                  "of (o, lse) + LSE combine",
+                   "parallelism": f"sequence shard x{ws}: partial attention + " + (
+                       "peer-memory exchange and LSE merge in one kernel (NVLink)"
+                       if xchg is not None else "NCCL all-gather of (o, lse) + LSE combine"),
                    "graph": graph is not None,
                    "l2": f"steps rotate over {layers} layer caches per rank"},
         "roofline": {"bound": "hbm", "achieved_per_gpu": round(value / ws, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(value / ws / peak, 4),
                      "peak_source": peak_kind},
         "clocks": clk.summary(),
-        "gpu_launches": args.steps * (1 if ws == 1 else 2),  # partial + combine per rank
+        "gpu_launches": args.steps * (1 if ws == 1 else 2),  # partial + exchange/combine
     }
 
 
@@ -731,6 +737,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--shard", choices=["batch", "seq"], default="batch",
                     help="seq: config-3 sequence sharding over the ranks (strong scaling)")
+    ap.add_argument("--seq-transport", choices=["peer", "allgather"], default="peer",
+                    help="--shard seq: partials over peer memory (one kernel) or NCCL")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
                     help="config2 = 8B decode at batch 16 (the headline); long* = batch-1 long context; "
                          "config4 = 70B shape, one KV head per GPU")

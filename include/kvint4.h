@@ -241,6 +241,31 @@ int kv4_lse_combine(const float *parts_o, const float *parts_lse, int64_t n_part
                     const kv4_tensor *out, void *stream);
 
 /*
+ * Sequence-shard exchange and merge in one launch, over peer memory (the
+ * step kv4_lse_combine takes after an all-gather, with no collective
+ * library and no host in the loop; capturable in a CUDA graph).  Every
+ * rank owns a buffer of kv4_lse_exchange_bytes(rows, d, world) bytes,
+ * zeroed before first use, reachable from every other rank's GPU
+ * (symmetric memory / CUDA IPC); peer_bufs is a DEVICE array of the
+ * world buffer addresses as seen from this GPU.  The kernel writes this
+ * rank's partial (part_o f32 [rows, d], part_lse f32 [rows], natural-log
+ * lse, as kv4_attention_partial emits them) into every buffer, each value
+ * paired with the call's epoch in one 8-byte store, waits until every
+ * rank's values carry the epoch (bounded: 2 s, then bit 4 of
+ * kv4_device_error is set and the merge proceeds on what is there) and
+ * writes the log-sum-exp merge to
+ * out [B, Hq, sq, d] (B*Hq*sq == rows).  state: this rank's two zeroed
+ * uint32 in device memory that count the calls (every rank makes the same
+ * calls in the same order; the count picks the flag value and which of
+ * two buffer halves a call uses).  No counterpart in the reference (it has
+ * no multi-GPU decode).
+ */
+int64_t kv4_lse_exchange_bytes(int64_t rows, int d, int world);
+int kv4_lse_exchange(const float *part_o, const float *part_lse, int64_t rows, int d,
+                     void *const *peer_bufs, int world, int rank, uint32_t *state,
+                     const kv4_tensor *out, void *stream);
+
+/*
  * kv4_attention without a workspace argument, for callers that cannot
  * allocate device memory at the call site (no allocator reachable from
  * their runtime, or a serving step that must not touch the allocator).  It

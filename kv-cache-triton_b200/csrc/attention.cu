@@ -2442,3 +2442,152 @@ extern "C" int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_pa
   return kv4_attention(q, k_packed, k_scales, v_packed, v_scales, out, group_size, is_causal,
                        sm_scale, scratch, kNoAllocScratchBytes, nullptr, stream);
 }
+
+// ===========================================================================
+// Sequence-shard exchange over peer memory (one kernel: push + merge)
+// ===========================================================================
+// Every rank holds a buffer of kv4_lse_exchange_bytes() bytes at the same
+// size on every GPU (e.g. symmetric memory), and a device array with the
+// addresses of all ranks' buffers as seen from this GPU.  Each value travels
+// with the call's epoch in one 8-byte store ({value bits, epoch}, written
+// and read as single 8-byte accesses), so a reader knows a value has
+// landed when its epoch matches: no fences and no separate flags.  Layout:
+//   uint2 [2][world][rows][d + 1]   (parity of the call, source rank, row,
+//                                    d values then the lse)
+// Call k uses parity k & 1: a rank can only be one call ahead of a peer
+// (its call k + 1 cannot end before the peer's call k values arrived, and
+// the peer pushes call k + 1 only after it read call k), so two parities keep
+// a slot from being overwritten while it is read.
+namespace kv4 {
+
+constexpr int kXBlocks = 64;                  // blocks of the exchange kernel (max)
+constexpr int DEV_ERR_PEER_TIMEOUT = 4;       // device error word bit
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // 2 s per call
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct XchgParams {
+  const float *po;
+  const float *pl;
+  int64_t rows;
+  int d;
+  void *const *peers;  // device array [world]
+  int world, rank;
+  uint32_t *state;  // this rank's [calls so far, blocks done] (device, zeroed once)
+  void *out;
+  int64_t os[4];
+  int out_dtype;
+  int64_t n1, n2;
+};
+
+__global__ void __launch_bounds__(256) kv4_lse_exchange_kernel(const XchgParams P) {
+  const int nb = gridDim.x, bid = blockIdx.x, tid = threadIdx.x;
+  // this call's epoch: calls so far + 1 (the last block of the call advances
+  // the count, so the next call, ordered after this one, sees it)
+  const uint32_t epoch = __ldcv(P.state) + 1u;
+  const int par = static_cast<int>(epoch & 1u);
+  const int64_t r0 = P.rows * bid / nb, r1 = P.rows * (bid + 1) / nb;
+  const int64_t rw = P.d + 1;                 // words per row
+  const int64_t slot = P.rows * rw;           // words per (parity, source)
+  auto at = [&](void *base, int src, int64_t r, int w) {
+    return reinterpret_cast<uint2 *>(base) + (static_cast<int64_t>(par) * P.world + src) * slot +
+           r * rw + w;
+  };
+  // 1. push this rank's rows [r0, r1) into slot `rank` of every rank's buffer
+  for (int q = 0; q < P.world; ++q) {
+    void *dst = P.peers[q];
+    for (int64_t i = tid; i < (r1 - r0) * rw; i += blockDim.x) {
+      const int64_t r = r0 + i / rw;
+      const int w = static_cast<int>(i - (r - r0) * rw);
+      const float v = w < P.d ? P.po[r * P.d + w] : P.pl[r];
+      asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(at(dst, P.rank, r, w)),
+                   "r"(__float_as_uint(v)), "r"(epoch)
+                   : "memory");
+    }
+  }
+  // 2. read every rank's rows [r0, r1) from this rank's buffer once they have
+  // landed (bounded wait), and merge them
+  void *mine = P.peers[P.rank];
+  const unsigned long long t0 = globaltimer_ns();
+  bool late = false;
+  auto fetch = [&](int src, int64_t r, int w) -> float {
+    uint32_t v, e;
+    while (true) {
+      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];"
+                   : "=r"(v), "=r"(e)
+                   : "l"(at(mine, src, r, w))
+                   : "memory");
+      if (e == epoch || late) break;
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        late = true;
+        atomicOr(&g_device_error, DEV_ERR_PEER_TIMEOUT);
+        break;
+      }
+    }
+    return __uint_as_float(v);
+  };
+  for (int64_t r = r0; r < r1; ++r) {
+    const int64_t i2 = r % P.n2, i01 = r / P.n2, i1 = i01 % P.n1, i0 = i01 / P.n1;
+    for (int dd = tid; dd < P.d; dd += blockDim.x) {
+      float M = kNegInf;
+      for (int k = 0; k < P.world; ++k) M = fmaxf(M, fetch(k, r, P.d));
+      float W = 0.0f, o = 0.0f;
+      for (int k = 0; k < P.world; ++k) {
+        const float l = fetch(k, r, P.d), v = fetch(k, r, dd);
+        const float w = (M == kNegInf) ? 0.0f : expf(l - M);
+        W += w;
+        o += w * v;
+      }
+      store_from_f32(P.out, P.out_dtype,
+                     i0 * P.os[0] + i1 * P.os[1] + i2 * P.os[2] + dd * P.os[3],
+                     W > 0.0f ? o / W : 0.0f);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {  // every block has read the epoch before the last one advances it
+    if (atomicAdd(&P.state[1], 1u) == static_cast<uint32_t>(nb) - 1u) {
+      P.state[1] = 0u;
+      __threadfence();
+      atomicExch(&P.state[0], epoch);
+    }
+  }
+}
+
+}  // namespace kv4
+
+extern "C" int64_t kv4_lse_exchange_bytes(int64_t rows, int d, int world) {
+  if (rows <= 0 || d <= 0 || world <= 0 || world > 64) return 0;
+  return 2 * static_cast<int64_t>(world) * rows * (d + 1) * 8;
+}
+
+extern "C" int kv4_lse_exchange(const float *part_o, const float *part_lse, int64_t rows,
+                                int d, void *const *peer_bufs, int world, int rank,
+                                uint32_t *state, const kv4_tensor *out, void *stream) {
+  if (!part_o || !part_lse || !peer_bufs || !out || !state || world <= 0 || world > 64 ||
+      rank < 0 || rank >= world || rows <= 0 || d <= 0)
+    return KV4_ERR_INVALID;
+  if (!is_float(out->dtype)) return KV4_ERR_DTYPE;
+  if (out->shape[0] * out->shape[1] * out->shape[2] != rows || out->shape[3] != d)
+    return KV4_ERR_SHAPE;
+  XchgParams P{};
+  P.po = part_o;
+  P.pl = part_lse;
+  P.rows = rows;
+  P.d = d;
+  P.peers = peer_bufs;
+  P.world = world;
+  P.rank = rank;
+  P.state = state;
+  P.out = out->data;
+  for (int i = 0; i < 4; ++i) P.os[i] = out->stride[i];
+  P.out_dtype = out->dtype;
+  P.n1 = out->shape[1];
+  P.n2 = out->shape[2];
+  const int nb = static_cast<int>(std::min<int64_t>(kXBlocks, rows));
+  kv4_lse_exchange_kernel<<<nb, 256, 0, static_cast<cudaStream_t>(stream)>>>(P);
+  return cuda_status(cudaGetLastError());
+}

@@ -27,6 +27,7 @@ EXPORTED = (
     "kv4_dequantize", "kv4_attention", "kv4_attention_plan", "kv4_attention_partial",
     "kv4_lse_combine", "kv4_device_error", "kv4_attention_noalloc", "kv4_append_attention",
     "kv4_attention_paged", "kv4_attention_paged_plan", "kv4_append_kv_paged",
+    "kv4_lse_exchange_bytes", "kv4_lse_exchange",
 )
 
 
@@ -107,6 +108,9 @@ def lib() -> ctypes.CDLL:
     L.kv4_attention_paged_plan.argtypes = [T, T, T, T, T, i64, i64, i32, P(AttnOpts),
                                            P(AttnPlan)]
     L.kv4_append_kv_paged.argtypes = [T, T, T, T, T, T, vp, i32, i32, vp]
+    L.kv4_lse_exchange_bytes.restype = i64
+    L.kv4_lse_exchange_bytes.argtypes = [i64, i32, i32]
+    L.kv4_lse_exchange.argtypes = [vp, vp, i64, i32, vp, i32, i32, vp, T, vp]
     for name in EXPORTED:
         if name not in ("kv4_version", "kv4_strerror", "kv4_last_cuda_error"):
             getattr(L, name).restype = i32

@@ -74,3 +74,33 @@ def test_four_sequence_shards_on_one_gpu_match_oracle():
     ref = oracle_attention(q, kp, ks, vp, vs, n_q_heads=32, n_kv_heads=8, group_size=32,
                            is_causal=True)
     np.testing.assert_allclose(f32(out), ref, atol=2e-2, rtol=0)
+
+
+def _free_port():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _run_exchange(world: int):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port",
+           str(_free_port()), os.path.join(ROOT, "tests", "exchange_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_peer_exchange_world1():
+    """kv4_lse_exchange with one rank (its own buffer as the only peer)."""
+    _run_exchange(1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_two_gpus():
+    """Sequence shards on two GPUs merged over peer memory, eagerly and from
+    a CUDA graph, equal the unsharded kernel."""
+    _run_exchange(2)
