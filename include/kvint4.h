@@ -72,7 +72,11 @@ typedef struct kv4_attn_opts {
   int32_t force_generic;   /* 1: use the generic (FFMA, any-stride) kernel */
   int32_t tiles_per_cta;   /* >0: override the split-K part length (tiles of 128 tokens per CTA) */
   int32_t max_ctas;        /* >0: cap the grid (CTAs of the one wave the split-K plan targets) */
-  int32_t reserved;
+  /* test knob: 1 = the fast path does not load each CTA's last tile and its
+     bounded waits give up after 16 polls of at most 1 ms, so the wait for that
+     tile expires: the kernel sets bit 1 of kv4_device_error, returns garbage
+     and leaves the context usable.  0 in normal use. */
+  int32_t debug_drop_last_tile;
 } kv4_attn_opts;
 
 /* Launch plan report (filled by kv4_attention_plan). */

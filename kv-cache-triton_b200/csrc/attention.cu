@@ -204,6 +204,8 @@ struct FastParams {
                   // [units][ngroups] first-level counters sit right before
   int units;
   int cs;         // > 1: launched as clusters of cs CTAs (consecutive parts of a unit)
+  int drop_last;  // test knob: the last tile of each CTA is never loaded
+  uint32_t wait_limit;  // polls of a bounded mbarrier wait (each <= 1 ms)
   const char *ks, *vs;         // scale tensors
   int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
   // Fused quantize-on-append (app_row >= 0): the new token's K/V rows
@@ -595,6 +597,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
       }
       return;
     }
+    if (P.drop_last && i == ntiles - 1) return;  // test knob: this tile never lands
     // packed codes: 2 tiled TMA loads (zero-filled past sk); scales: one bulk
     // copy per tensor of the tile's contiguous rows, rounded up to 16 bytes
     const int rem = min(TOK, C.sk - t0);
@@ -1125,7 +1128,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     if (++stage == Cfg::STAGES) stage = 0;
     if (stage == 0) phase ^= 1u;
     if (!*reinterpret_cast<volatile int *>(&sh_abort) &&
-        !mbar_wait_bounded(bar_base + 8 * stage, phase)) {
+        !mbar_wait_bounded(bar_base + 8 * stage, phase, P.wait_limit)) {
       atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
       sh_abort = 1;  // later waits are skipped; results are garbage, the flag reports it
     }
@@ -1597,7 +1600,7 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     // drain: wait (bounded) for the loads this CTA may still have in flight
     for (int i = max(0, ntiles - Cfg::STAGES); i < ntiles; ++i) {
       const int s = i % Cfg::STAGES;
-      mbar_wait_bounded(bar_base + 8 * s, (i / Cfg::STAGES) & 1, 1u << 16);
+      mbar_wait_bounded(bar_base + 8 * s, (i / Cfg::STAGES) & 1, 4 * P.wait_limit);
     }
   }
 }
@@ -2195,6 +2198,8 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
                               : nullptr;
     FP.units = pl.units;
     FP.cs = pl.cs;
+    FP.drop_last = (opts && opts->debug_drop_last_tile) ? 1 : 0;
+    FP.wait_limit = FP.drop_last ? 16u : (1u << 14);
     FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) *
                                             (pl.maxp + merge_groups(pl.maxp)) * NCOL * pl.D
                             : nullptr;

@@ -46,7 +46,7 @@ class AttnOpts(ctypes.Structure):
         ("force_generic", ctypes.c_int32),
         ("tiles_per_cta", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("debug_drop_last_tile", ctypes.c_int32),
     ]
 
 

@@ -131,13 +131,14 @@ def _workspace(dev: torch.device, plan: AttnPlan) -> torch.Tensor | None:
     return buf
 
 
-def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0):
-    if not (force_generic or tiles_per_cta or max_ctas):
+def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0, debug_drop_last_tile=False):
+    if not (force_generic or tiles_per_cta or max_ctas or debug_drop_last_tile):
         return None
     o = AttnOpts()
     o.force_generic = int(bool(force_generic))
     o.tiles_per_cta = int(tiles_per_cta)
     o.max_ctas = int(max_ctas)
+    o.debug_drop_last_tile = int(bool(debug_drop_last_tile))
     return o
 
 
