@@ -189,6 +189,22 @@ def _with_workspace(dev: torch.device, call, ds, group_size, is_causal, optr) ->
     return rc
 
 
+_DESC_MEMO: dict = {}
+
+
+def _desc_ref(t: torch.Tensor):
+    """``byref`` of a descriptor of ``t``, memoised on (address, dtype, shape,
+    strides): a decode loop passes the same activation buffers every step."""
+    key = (t.data_ptr(), t.dtype, t.shape, t.stride())
+    r = _DESC_MEMO.get(key)
+    if r is None:
+        if len(_DESC_MEMO) > 512:
+            _DESC_MEMO.clear()
+        d = desc(t)
+        r = _DESC_MEMO[key] = (d, ctypes.byref(d))
+    return r[1]
+
+
 @_on_device
 def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
                            is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
@@ -196,18 +212,21 @@ def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
     """``append_attention_into`` with prebuilt descriptors of the four cache
     views (a decode loop keeps them per layer and only updates the length)."""
     L = lib()
-    dq, dkn, dvn, do = desc(q), desc(k_new), desc(v_new), desc(out)
-    ds = [dq, *cache_descs, do]
-    refs = [ctypes.byref(d) for d in ds]
+    rq, rk, rv, ro = _desc_ref(q), _desc_ref(k_new), _desc_ref(v_new), _desc_ref(out)
     st = _stream(q.device)
+    buf = _WS.get((q.device.index, st), (None, 0))[0]
+    args = (rq, rk, rv, *[ctypes.byref(d) for d in cache_descs], ro, int(group_size),
+            int(tie_mode), int(is_causal), float(sm_scale))
+    rc = L.kv4_append_attention(*args, buf.data_ptr() if buf is not None else None,
+                                buf.numel() if buf is not None else 0, None, st)
+    if rc == _lib.KV4_ERR_WORKSPACE:  # first call on this stream: size the workspace
+        ds = [desc(q), *cache_descs, desc(out)]
 
-    def call(ws, nbytes):
-        return L.kv4_append_attention(refs[0], ctypes.byref(dkn), ctypes.byref(dvn), *refs[1:],
-                                      int(group_size), int(tie_mode), int(is_causal),
-                                      float(sm_scale), ws, nbytes, None, st)
+        def call(ws, nbytes):
+            return L.kv4_append_attention(*args, ws, nbytes, None, st)
 
-    check("kv4_append_attention",
-          _with_workspace(q.device, call, ds, group_size, is_causal, None))
+        rc = _with_workspace(q.device, call, ds, group_size, is_causal, None)
+    check("kv4_append_attention", rc)
 
 
 @_on_device
