@@ -491,7 +491,69 @@ def extra_workloads(dev, with_reference=True):
             del store, q
             torch.cuda.empty_cache()
     res["sweep_b1_32q_8kv_d128"] = sweeps
+    res["prefill_b1_32q_8kv_d128"] = prefill_workloads(dev, ref_fn)
     return res
+
+
+def _bf16_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_workloads(dev, ref_fn=None):
+    """Causal prefill attention over the packed cache (one layer, B=1, 32/8
+    heads, d=128, G=32, sq = sk): the tensor-core kernel
+    (``kv4_prefill_attention``) beside the dequantize + flash-attention route
+    and the reference's Triton kernel.  FLOPs counted as 4 * Hq * d * (number
+    of visible (query, key) pairs)."""
+    from kvint4 import frontend, ops
+    st = torch.cuda.current_stream(dev)
+    peak, kind = _bf16_peak()
+    rows = []
+    for s_ in (2048, 8192, 16384):
+        with workload_dims(B=1, HQ=32, HKV=8, S=s_, G=32, LAYERS=2):
+            store, _, _, _ = build_caches(dev)
+            g = torch.Generator(device=dev).manual_seed(5)
+            q = torch.randn(LAYERS, B, HQ, S, D, device=dev, generator=g).to(torch.bfloat16)
+            out = torch.empty(B, HQ, S, D, dtype=torch.bfloat16, device=dev)
+            pairs = B * S * (S + 1) // 2
+            flops = 4.0 * HQ * D * pairs
+
+            def ours(l):
+                ops.prefill_attention_into(q[l], *store.layer(l).views(), out, G, True)
+
+            def sdpa(l):
+                frontend._prefill_sdpa(q[l], *store.layer(l).views(), G, True, out)
+
+            us = _graph_time_us(ours, LAYERS, 4, st)
+            row = {"seq_len": S, "ours_us": round(us, 1),
+                   "ours_TFLOP/s": round(flops / (us * 1e-6) / 1e12, 1),
+                   "frac_of_bf16_peak": round(flops / (us * 1e-6) / 1e12 / peak, 3),
+                   "peak_kind": kind}
+            try:
+                dus = _graph_time_us(sdpa, LAYERS, 4, st)
+                row["dequant_sdpa_us"] = round(dus, 1)
+                row["speedup_vs_dequant_sdpa"] = round(dus / us, 2)
+            except Exception as e:  # noqa: BLE001
+                row["dequant_sdpa"] = f"unavailable: {type(e).__name__}"
+            if ref_fn is not None:
+                try:
+                    def ref(l):
+                        ref_fn(q[l], *store.layer(l).views(), n_q_heads=HQ, n_kv_heads=HKV,
+                               group_size=G, is_causal=True)
+
+                    rus = _graph_time_us(ref, LAYERS, 2, st)
+                    row["reference_triton_us"] = round(rus, 1)
+                    row["speedup_vs_reference"] = round(rus / us, 2)
+                except Exception as e:  # noqa: BLE001
+                    row["reference_triton"] = f"unavailable: {type(e).__name__}"
+            rows.append(row)
+            del store, q, out
+            torch.cuda.empty_cache()
+    return rows
 
 
 def triton_reference_leg(store, q, span, reps, warmup, st):

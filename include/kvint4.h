@@ -289,7 +289,31 @@ int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_packed,
                           const kv4_tensor *v_scales, const kv4_tensor *out, int group_size,
                           int is_causal, float sm_scale, void *stream);
 
-/* Read-and-clear the device error word that bounded waits set (synchronizes the stream). */
+/*
+ * Fused prefill attention on the tensor cores (tcgen05, tensor-memory
+ * accumulators): the same result as kv4_attention for a query block, with
+ * K/V dequantized tile by tile in shared memory (never written to HBM).
+ * Supported: q/out/scales bf16, d == 128, packed rows of exactly 64 bytes
+ * (token stride 64, 16-byte aligned planes and batch/head strides), scales
+ * [.., d/G] contiguous per token, G in {16, 32, 64, 128}, 128 % (Hq/Hkv) == 0,
+ * B * Hkv <= 65535, and for is_causal sq <= sk (bottom-right alignment:
+ * query i sees keys j <= sk - sq + i).  Anything else returns
+ * KV4_ERR_UNSUPPORTED / KV4_ERR_LAYOUT and the caller uses kv4_attention.
+ * sm_scale <= 0 means 1/sqrt(d).  No workspace.  The tensor-core operands
+ * are f16: dequantized K/V values are exact in f16 while |value| < 65504;
+ * a scale above 65504/8 sets bit 8 of kv4_device_error (output not valid).
+ * Replaces the prefill branch (sq > 1) of kernels/llama3/attention_quant.py:24-152
+ * (_attn_fwd_quant_gqa_kernel with IS_CAUSAL) for the shapes above.
+ */
+int kv4_prefill_attention(const kv4_tensor *q, const kv4_tensor *k_packed,
+                          const kv4_tensor *k_scales, const kv4_tensor *v_packed,
+                          const kv4_tensor *v_scales, const kv4_tensor *out, int group_size,
+                          int is_causal, float sm_scale, void *stream);
+
+/* Read-and-clear the device error word (synchronizes the stream): bit 1 a
+   bounded mbarrier wait expired, bit 2 a page id outside the pool, bit 4 a
+   peer exchange wait expired, bit 8 kv4_prefill_attention met K/V values
+   outside the f16 range. */
 int kv4_device_error(void *stream, int *flag_out);
 
 #ifdef __cplusplus

@@ -2355,6 +2355,10 @@ extern "C" int kv4_lse_combine(const float *parts_o, const float *parts_lse, int
   return cuda_status(cudaGetLastError());
 }
 
+namespace kv4 {
+int prefill_take_device_error(int *v);  // prefill.cu
+}
+
 extern "C" int kv4_device_error(void *stream, int *flag_out) {
   if (!flag_out) return KV4_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -2364,7 +2368,10 @@ extern "C" int kv4_device_error(void *stream, int *flag_out) {
   rc = cuda_status(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
   if (rc) return rc;
   rc = cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
-  *flag_out = v;
+  if (rc) return rc;
+  int pv = 0;
+  rc = prefill_take_device_error(&pv);
+  *flag_out = v | pv;
   return rc;
 }
 
@@ -2466,7 +2473,6 @@ extern "C" int kv4_attention_noalloc(const kv4_tensor *q, const kv4_tensor *k_pa
 namespace kv4 {
 
 constexpr int kXBlocks = 64;                  // blocks of the exchange kernel (max)
-constexpr int DEV_ERR_PEER_TIMEOUT = 4;       // device error word bit
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // 2 s per call
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

@@ -16,7 +16,12 @@ namespace kv4 {
 void set_cuda_error(cudaError_t e);
 int cuda_status(cudaError_t e);  // KV4_OK or KV4_ERR_CUDA (records the string)
 
-enum DeviceErr : int { DEV_ERR_MBAR_TIMEOUT = 1, DEV_ERR_BAD_PAGE = 2 };
+enum DeviceErr : int {
+  DEV_ERR_MBAR_TIMEOUT = 1,
+  DEV_ERR_BAD_PAGE = 2,
+  DEV_ERR_PEER_TIMEOUT = 4,  // a peer exchange wait expired
+  DEV_ERR_F16_RANGE = 8       // prefill: K/V values outside the f16 operand range
+};
 
 // ---------------------------------------------------------------------------
 // scalar conversions

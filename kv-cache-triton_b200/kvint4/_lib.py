@@ -27,7 +27,7 @@ EXPORTED = (
     "kv4_dequantize", "kv4_attention", "kv4_attention_plan", "kv4_attention_partial",
     "kv4_lse_combine", "kv4_device_error", "kv4_attention_noalloc", "kv4_append_attention",
     "kv4_attention_paged", "kv4_attention_paged_plan", "kv4_append_kv_paged",
-    "kv4_lse_exchange_bytes", "kv4_lse_exchange",
+    "kv4_lse_exchange_bytes", "kv4_lse_exchange", "kv4_prefill_attention",
 )
 
 
@@ -101,6 +101,7 @@ def lib() -> ctypes.CDLL:
     L.kv4_lse_combine.argtypes = [vp, vp, i64, T, vp]
     L.kv4_device_error.argtypes = [vp, P(ctypes.c_int)]
     L.kv4_attention_noalloc.argtypes = [T, T, T, T, T, T, i32, i32, f32, vp]
+    L.kv4_prefill_attention.argtypes = [T, T, T, T, T, T, i32, i32, f32, vp]
     L.kv4_append_attention.argtypes = [T, T, T, T, T, T, T, T, i32, i32, i32, f32, vp, sz,
                                        P(AttnOpts), vp]
     L.kv4_attention_paged.argtypes = [T, T, T, T, T, vp, i64, i64, vp, i64, T, i32, i32, f32, vp,

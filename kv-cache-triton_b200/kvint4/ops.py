@@ -170,6 +170,22 @@ def attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = Fa
     check("kv4_attention", _with_workspace(q.device, call, ds, group_size, is_causal, optr))
 
 
+@_on_device
+def prefill_attention_into(q, kp, ks, vp, vs, out, group_size: int, is_causal: bool = False,
+                           sm_scale: float = 0.0, *, strict: bool = True) -> bool:
+    """Tensor-core prefill kernel (``kv4_prefill_attention``).  Returns False
+    when the shape or layout is outside what the kernel takes (only with
+    ``strict=False``; otherwise that raises ``Kv4Error``)."""
+    L = lib()
+    refs = [ctypes.byref(desc(t)) for t in (q, kp, ks, vp, vs, out)]
+    rc = L.kv4_prefill_attention(*refs, int(group_size), int(is_causal), float(sm_scale),
+                                 _stream(q.device))
+    if not strict and rc in (_lib.KV4_ERR_UNSUPPORTED, _lib.KV4_ERR_LAYOUT, _lib.KV4_ERR_DTYPE):
+        return False
+    check("kv4_prefill_attention", rc)
+    return True
+
+
 def _with_workspace(dev: torch.device, call, ds, group_size, is_causal, optr) -> int:
     """Run ``call(ws_ptr, ws_bytes)`` with this (device, stream)'s workspace.
     The common case plans nothing: the library reports KV4_ERR_WORKSPACE
