@@ -223,9 +223,12 @@ def run_ours(args, ws, rank, local):
         kp, ks, vp, vs = store.layer(l).views()
         ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
 
-    def step_op(l):  # the product's decode step: append fused into the attention launch
+    def step_op(l, early=True):  # the product's decode step: append fused into the attention
+        # launch, started early behind the previous layer's step (the cache
+        # layer's own decode loop does the same: kv4_attn_opts.early_start)
         kp, ks, vp, vs = store.layer(l).views()
-        ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False)
+        ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False,
+                                  early_start=early)
 
     for l in range(LAYERS):
         store.layer(l).seq_len = S
@@ -252,6 +255,10 @@ def run_ours(args, ws, rank, local):
         for l in range(span):
             append_op(l)
             attn_op(l)
+    g_all_plain = torch.cuda.CUDAGraph()  # fused steps in plain stream order
+    with torch.cuda.graph(g_all_plain):
+        for l in range(span):
+            step_op(l, early=False)
     reps = args.steps // span
 
     for _ in range(max(1, -(-args.warmup // span))):
@@ -283,6 +290,15 @@ def run_ours(args, ws, rank, local):
     p1.record(st)
     torch.cuda.synchronize()
     pair_ms = p0.elapsed_time(p1)
+    for _ in range(max(1, -(-args.warmup // span))):
+        g_all_plain.replay()
+    torch.cuda.synchronize()
+    p0.record(st)
+    for _ in range(reps):
+        g_all_plain.replay()
+    p1.record(st)
+    torch.cuda.synchronize()
+    plain_ms = p0.elapsed_time(p1)
     gpu_ref = None
     if not args.no_gpu_reference and ws == 1:
         gpu_ref = triton_reference_leg(store, q, span, reps, args.warmup, st)
@@ -325,11 +341,11 @@ def run_ours(args, ws, rank, local):
     e2e_ms = e0.elapsed_time(e1)
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms, pair_ms], device=dev)
+    t = torch.tensor([ms, e2e_ms, pair_ms, plain_ms], device=dev)
     if ws > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.barrier()
-    ms, e2e_ms, pair_ms = (float(x) for x in t.tolist())
+    ms, e2e_ms, pair_ms, plain_ms = (float(x) for x in t.tolist())
     # the timed region holds only the fused kernel, one launch per step: its
     # average launch duration is the region's time / launches
     attn_avg_ms = ms / (args.steps * int(p.kernels))
@@ -366,6 +382,7 @@ def run_ours(args, ws, rank, local):
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "kernel_us": round(attn_avg_ms * 1e3, 2),
                      "unfused_append_plus_attention_us": round(pair_avg_ms * 1e3, 2),
+                     "plain_stream_order_us": round(plain_ms * 1e3 / args.steps, 2),
                      # DRAM bytes come from an ncu capture, not from this run
                      "traffic": None},
         "clocks": clk.summary(),
@@ -447,7 +464,8 @@ def extra_workloads(dev, with_reference=True):
 
             def step(l):
                 kp, ks, vp, vs = store.layer(l).views()
-                ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False)
+                ops.append_attention_into(q[l], kn[l], vn[l], kp, ks, vp, vs, out, G, False,
+                                          early_start=True)
 
             with ClockSampler(dev.index or 0) as clk:
                 us = _graph_time_us(step, LAYERS, max(2, 64 // LAYERS), st)
@@ -469,7 +487,7 @@ def extra_workloads(dev, with_reference=True):
 
             def attn(l):
                 kp, ks, vp, vs = store.layer(l).views()
-                ops.attention_into(q[l], kp, ks, vp, vs, out, G, False)
+                ops.attention_into(q[l], kp, ks, vp, vs, out, G, False, early_start=True)
 
             us = _graph_time_us(attn, LAYERS, max(2, 128 // LAYERS), st)
             row = {"seq_len": S, "group_size": G, "layer_copies": LAYERS,

@@ -77,6 +77,16 @@ typedef struct kv4_attn_opts {
      tile expires: the kernel sets bit 1 of kv4_device_error, returns garbage
      and leaves the context usable.  0 in normal use. */
   int32_t debug_drop_last_tile;
+  /* 1: launch the tensor-core kernel with programmatic stream serialization,
+     so that it starts (barrier set-up, the first cache tiles in flight) while
+     the kernel before it on the stream drains; it reads q, the new row, the
+     workspace and writes anything only after that kernel has completed.
+     Contract: the kernel launched immediately before this call on `stream`
+     writes no row of this call's cache views, except row S-2 when this call
+     appends row S-1 (a fused decode step on the same layer right after the
+     previous one).  Ignored for the paged layout and when the call appends
+     through the separate quantize kernel.  0 = ordinary stream order. */
+  int32_t early_start;
 } kv4_attn_opts;
 
 /* Launch plan report (filled by kv4_attention_plan). */

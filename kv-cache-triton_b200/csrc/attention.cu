@@ -205,6 +205,7 @@ struct FastParams {
   int units;
   int cs;         // > 1: launched as clusters of cs CTAs (consecutive parts of a unit)
   int drop_last;  // test knob: the last tile of each CTA is never loaded
+  int early;      // launched with programmatic stream serialization (see the kernel)
   uint32_t wait_limit;  // polls of a bounded mbarrier wait (each <= 1 ms)
   const char *ks, *vs;         // scale tensors
   int64_t ks_sb, ks_sh, vs_sb, vs_sh;  // their batch / head strides in bytes
@@ -525,12 +526,22 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
       (reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(C.q) + q_base + 8 * tg) &
        15) == 0;
   uint4 q_raw[NCH];
-  if (q_vec) {
+  auto load_q = [&]() {
+    if (q_vec) {
 #pragma unroll
-    for (int c = 0; c < NCH; ++c)
-      q_raw[c] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(C.q) +
-                                                       q_base + 32 * c + 8 * tg));
-  }
+      for (int c = 0; c < NCH; ++c)
+        q_raw[c] = __ldg(reinterpret_cast<const uint4 *>(
+            static_cast<const __nv_bfloat16 *>(C.q) + q_base + 32 * c + 8 * tg));
+    }
+  };
+  // Early start (P.early, launched with programmatic stream serialization):
+  // until griddepcontrol.wait returns, the kernel reads only cache tiles that
+  // the preceding kernel cannot be writing (host contract: it writes at most
+  // row app_row - 1 of these views; the tile holding that row waits) and
+  // writes nothing outside shared memory.  q, the new row, the workspace and
+  // the output are touched after the wait.
+  const bool early = P.early != 0 && !paged;
+  if (!early) load_q();
 
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
@@ -610,8 +621,19 @@ __global__ void __launch_bounds__(128, (D == 256 ? 2 : KV4_MINB))
     bulk_load(dst + 2 * Cfg::KP + Cfg::KS, P.vs + b * P.vs_sb + kvh * P.vs_sh + soff, sbytes, bar);
   };
 
-  if (tid == 0) {
-    const int pre = min(ntiles, Cfg::STAGES);
+  const int pre = min(ntiles, Cfg::STAGES);
+  if (early) {
+    // tiles of this CTA's first stages that cannot hold row app_row - 1 load
+    // before the wait; the rest (at most one tile) after it
+    const int hot = P.app_row > 0 ? (P.app_row - 1) / TOK - t_begin : -1;
+    if (tid == 0)
+      for (int i = 0; i < pre; ++i)
+        if (i != hot) issue(i);
+    griddep_wait();
+    griddep_launch_dependents();
+    load_q();
+    if (tid == 0 && hot >= 0 && hot < pre) issue(hot);
+  } else if (tid == 0) {
     for (int i = 0; i < pre; ++i) issue(i);
   }
 
@@ -1782,9 +1804,13 @@ static int fast_occupancy(int D, int G, int sdt, int mode) {
   KV4_OCC(64, 32, STT) KV4_OCC(64, 64, STT) KV4_OCC(128, 32, STT) KV4_OCC(128, 64, STT) \
       KV4_OCC(128, 128, STT) KV4_OCC(256, 32, STT) KV4_OCC(256, 64, STT)              \
           KV4_OCC(256, 128, STT)
+#ifdef KV4_DEV_SUBSET
+  if (sdt == KV4_BF16) { KV4_OCC(128, 32, __nv_bfloat16) }
+#else
   if (sdt == KV4_BF16) { KV4_OCC_S(__nv_bfloat16) }
   else if (sdt == KV4_F16) { KV4_OCC_S(__half) }
   else { KV4_OCC_S(float) }
+#endif
 #undef KV4_OCC_S
 #undef KV4_OCC
   return 1;
@@ -1947,19 +1973,28 @@ static int launch_fast_t(const FastParams &FP, const Plan &pl, const kv4_tensor 
       }
     }
   }
-  if (FP.cs > 1) {  // the split-K parts of a unit merge inside a thread-block cluster
+  if (FP.cs > 1 || FP.early) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(pl.ctas));
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(FP.cs);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    unsigned na = 0;
+    if (FP.cs > 1) {  // the split-K parts of a unit merge inside a thread-block cluster
+      attr[na].id = cudaLaunchAttributeClusterDimension;
+      attr[na].val.clusterDim.x = static_cast<unsigned>(FP.cs);
+      attr[na].val.clusterDim.y = 1;
+      attr[na].val.clusterDim.z = 1;
+      ++na;
+    }
+    if (FP.early) {  // may start while the previous kernel in the stream drains
+      attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[na].val.programmaticStreamSerializationAllowed = 1;
+      ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = na;
     rc = cuda_status(cudaLaunchKernelEx(&cfg, kv4_attn_fast<D, G, ST, MODE, PAGED>, FP, tkp, tvp));
     if (rc) return rc;
   } else {
@@ -1991,8 +2026,12 @@ static int launch_fast_st(const FastParams &FP, const Plan &pl, const kv4_tensor
   const int D = pl.D, G = FP.c.G;
 #define KV4_L(DD, GG) \
   if (D == DD && G == GG) return launch_fast_s<DD, GG, ST>(FP, pl, kp, ks, vp, vs, st);
+#ifdef KV4_DEV_SUBSET  // development builds: the Llama decode shape only
+  KV4_L(128, 32)
+#else
   KV4_L(64, 32) KV4_L(64, 64) KV4_L(128, 32) KV4_L(128, 64) KV4_L(128, 128) KV4_L(256, 32)
       KV4_L(256, 64) KV4_L(256, 128)
+#endif
 #undef KV4_L
   return KV4_ERR_UNSUPPORTED;
 }
@@ -2199,13 +2238,19 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
     FP.units = pl.units;
     FP.cs = pl.cs;
     FP.drop_last = (opts && opts->debug_drop_last_tile) ? 1 : 0;
+    // (not behind the separate append kernel this call launches itself)
+    FP.early = (opts && opts->early_start && FP.page == 0 && !(app && !fuse_app)) ? 1 : 0;
     FP.wait_limit = FP.drop_last ? 16u : (1u << 14);
     FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) *
                                             (pl.maxp + merge_groups(pl.maxp)) * NCOL * pl.D
                             : nullptr;
     if (pl.sdt == KV4_BF16) return launch_fast_st<__nv_bfloat16>(FP, pl, kp, ks, vp, vs, st);
+#ifndef KV4_DEV_SUBSET
     if (pl.sdt == KV4_F16) return launch_fast_st<__half>(FP, pl, kp, ks, vp, vs, st);
     return launch_fast_st<float>(FP, pl, kp, ks, vp, vs, st);
+#else
+    return KV4_ERR_UNSUPPORTED;
+#endif
   }
   // generic
   GenParams GP{};

@@ -47,6 +47,7 @@ class AttnOpts(ctypes.Structure):
         ("tiles_per_cta", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
         ("debug_drop_last_tile", ctypes.c_int32),
+        ("early_start", ctypes.c_int32),
     ]
 
 

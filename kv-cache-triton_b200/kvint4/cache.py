@@ -39,6 +39,10 @@ class LayerStore:
     v_packed_buf: torch.Tensor
     v_scales_buf: torch.Tensor
     seq_len: int
+    # True while the last kernel that wrote these buffers was a fused decode
+    # step (kv4_append_attention): the next fused step may then start early
+    # (kv4_attn_opts.early_start), since no other kernel wrote the rows it reads
+    early_ok: bool = False
 
     @property
     def capacity(self) -> int:
@@ -101,6 +105,7 @@ class Int4KVStore:
                       layer.v_packed_buf, layer.v_scales_buf, layer.seq_len, self.group_size,
                       self.tie_mode)
         layer.seq_len += s
+        layer.early_ok = False
 
     def append_attend(self, query: torch.Tensor, key_states: torch.Tensor,
                       value_states: torch.Tensor, layer_idx: int, out: torch.Tensor, *,
@@ -119,8 +124,10 @@ class Int4KVStore:
                                       is_causal=is_causal, out=out)
         n = layer.seq_len + 1
         ops.append_attention_descs(query, key_states, value_states, layer.view_descs(n), out,
-                                   self.group_size, is_causal, self.tie_mode)
+                                   self.group_size, is_causal, self.tie_mode,
+                                   early_start=layer.early_ok)
         layer.seq_len = n
+        layer.early_ok = True
         return out
 
     def _reserve(self, key_states: torch.Tensor, value_states: torch.Tensor,
@@ -172,6 +179,7 @@ class Int4KVStore:
             idx = beam_idx.to(st.k_packed_buf.device)
             for name in ("k_packed_buf", "k_scales_buf", "v_packed_buf", "v_scales_buf"):
                 setattr(st, name, getattr(st, name).index_select(0, idx).contiguous())
+            st.early_ok = False
 
     def layer(self, layer_idx: int) -> LayerStore:
         st = self._layers.get(layer_idx)

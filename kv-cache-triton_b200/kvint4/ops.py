@@ -131,15 +131,22 @@ def _workspace(dev: torch.device, plan: AttnPlan) -> torch.Tensor | None:
     return buf
 
 
-def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0, debug_drop_last_tile=False):
-    if not (force_generic or tiles_per_cta or max_ctas or debug_drop_last_tile):
+def _opts(force_generic=False, tiles_per_cta=0, max_ctas=0, debug_drop_last_tile=False,
+          early_start=False):
+    if not (force_generic or tiles_per_cta or max_ctas or debug_drop_last_tile or early_start):
         return None
     o = AttnOpts()
     o.force_generic = int(bool(force_generic))
     o.tiles_per_cta = int(tiles_per_cta)
     o.max_ctas = int(max_ctas)
     o.debug_drop_last_tile = int(bool(debug_drop_last_tile))
+    o.early_start = int(bool(early_start))
     return o
+
+
+_EARLY = AttnOpts()
+_EARLY.early_start = 1
+_EARLY_REF = ctypes.byref(_EARLY)
 
 
 def plan(q, kp, ks, vp, vs, out, group_size, is_causal=False, **kw) -> AttnPlan:
@@ -224,24 +231,28 @@ def _desc_ref(t: torch.Tensor):
 @_on_device
 def append_attention_descs(q, k_new, v_new, cache_descs, out, group_size: int,
                            is_causal: bool = False, tie_mode: int = _lib.TIE_HALF_AWAY,
-                           sm_scale: float = 0.0) -> None:
+                           sm_scale: float = 0.0, early_start: bool = False) -> None:
     """``append_attention_into`` with prebuilt descriptors of the four cache
-    views (a decode loop keeps them per layer and only updates the length)."""
+    views (a decode loop keeps them per layer and only updates the length).
+    ``early_start``: the caller guarantees the kernel launched just before on
+    the stream writes no row of these views except the previous decode row
+    (``kv4_attn_opts.early_start``)."""
     L = lib()
     rq, rk, rv, ro = _desc_ref(q), _desc_ref(k_new), _desc_ref(v_new), _desc_ref(out)
     st = _stream(q.device)
     buf = _WS.get((q.device.index, st), (None, 0))[0]
     args = (rq, rk, rv, *[ctypes.byref(d) for d in cache_descs], ro, int(group_size),
             int(tie_mode), int(is_causal), float(sm_scale))
+    optr = _EARLY_REF if early_start else None
     rc = L.kv4_append_attention(*args, buf.data_ptr() if buf is not None else None,
-                                buf.numel() if buf is not None else 0, None, st)
+                                buf.numel() if buf is not None else 0, optr, st)
     if rc == _lib.KV4_ERR_WORKSPACE:  # first call on this stream: size the workspace
         ds = [desc(q), *cache_descs, desc(out)]
 
         def call(ws, nbytes):
-            return L.kv4_append_attention(*args, ws, nbytes, None, st)
+            return L.kv4_append_attention(*args, ws, nbytes, optr, st)
 
-        rc = _with_workspace(q.device, call, ds, group_size, is_causal, None)
+        rc = _with_workspace(q.device, call, ds, group_size, is_causal, optr)
     check("kv4_append_attention", rc)
 
 
