@@ -269,6 +269,7 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        _hold(st)
         t0.record(st)
         for _ in range(reps):
             g_all.replay()
@@ -284,6 +285,7 @@ def run_ours(args, ws, rank, local):
         g_all_pair.replay()
     torch.cuda.synchronize()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _hold(st)
     p0.record(st)
     for _ in range(reps):
         g_all_pair.replay()
@@ -293,6 +295,7 @@ def run_ours(args, ws, rank, local):
     for _ in range(max(1, -(-args.warmup // span))):
         g_all_plain.replay()
     torch.cuda.synchronize()
+    _hold(st)
     p0.record(st)
     for _ in range(reps):
         g_all_plain.replay()
@@ -417,6 +420,14 @@ class workload_dims:
         globals().update(self.saved)
 
 
+def _hold(st=None):
+    """Keep the stream busy for about 1 ms (a device-side spin) before a timed
+    region starts, so that the region's first event and the launches behind
+    it are all queued before the GPU reaches them: the region then measures
+    device time only, not the host's launch latency or a thread switch."""
+    torch.cuda._sleep(2_000_000)
+
+
 def _graph_time_us(step, span, reps, st):
     """Device time per step of `reps` replays of a graph of `span` steps."""
     for l in range(span):
@@ -430,6 +441,7 @@ def _graph_time_us(step, span, reps, st):
     graph.replay()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _hold(st)
     t0.record(st)
     for _ in range(reps):
         graph.replay()
@@ -601,6 +613,7 @@ def triton_reference_leg(store, q, span, reps, warmup, st):
             graph.replay()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _hold(st)
         t0.record(st)
         for _ in range(reps):
             graph.replay()
@@ -764,6 +777,7 @@ def run_seq_shard(args, ws, rank, local):
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        _hold(st)
         t0.record(st)
         run_steps(args.steps)
         t1.record(st)

@@ -84,8 +84,10 @@ typedef struct kv4_attn_opts {
      Contract: the kernel launched immediately before this call on `stream`
      writes no row of this call's cache views, except row S-2 when this call
      appends row S-1 (a fused decode step on the same layer right after the
-     previous one).  Ignored for the paged layout and when the call appends
-     through the separate quantize kernel.  0 = ordinary stream order. */
+     previous one).  Ignored for the paged layout, when the call appends
+     through the separate quantize kernel, and for plans of long split-K parts
+     merged inside a thread-block cluster (nothing to overlap there).
+     0 = ordinary stream order. */
   int32_t early_start;
 } kv4_attn_opts;
 

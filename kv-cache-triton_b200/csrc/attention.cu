@@ -1867,8 +1867,11 @@ static void make_plan(const kv4_tensor *q, const kv4_tensor *kp, const kv4_tenso
     int64_t k = std::max<int64_t>(1, target / pl.units);
     // at least 4 tiles per CTA: shorter parts spend more time in their
     // prologue and merge than in streaming (measured: batch-1 16K context
-    // takes 17.5 us with 32 parts of 4 tiles, 24 us with 74 parts)
-    k = std::min<int64_t>(k, std::max<int64_t>(1, pl.tpu / 4));
+    // takes 17.5 us with 32 parts of 4 tiles, 24 us with 74 parts) -- except
+    // that up to 8 parts of >= 2 tiles, which merge inside one cluster, pay
+    // (measured: batch-1 2K context 9.7 us with 4 parts, 7.9 us with 8)
+    k = std::min<int64_t>(
+        k, std::max<int64_t>({1, pl.tpu / 4, std::min<int64_t>(kMaxCluster, pl.tpu / 2)}));
     if (opts && opts->tiles_per_cta > 0) k = (pl.tpu + opts->tiles_per_cta - 1) / opts->tiles_per_cta;
     k = std::min<int64_t>(k, pl.tpu);
     pl.cs = cluster_size_of(k);
@@ -2240,6 +2243,11 @@ static int run_attention(const kv4_tensor *q, const kv4_tensor *kp, const kv4_te
     FP.drop_last = (opts && opts->debug_drop_last_tile) ? 1 : 0;
     // (not behind the separate append kernel this call launches itself)
     FP.early = (opts && opts->early_start && FP.page == 0 && !(app && !fuse_app)) ? 1 : 0;
+    // long parts merged inside a cluster leave no head or tail worth
+    // overlapping (measured: the 8B batch-16 step, 3 parts of 11 tiles, was
+    // 0.6 us slower with early start; every global-merge or short-part plan
+    // measured faster)
+    if (pl.cs > 1 && pl.L >= 8) FP.early = 0;
     FP.wait_limit = FP.drop_last ? 16u : (1u << 14);
     FP.ws_lse = pl.ws_bytes ? FP.ws_o + static_cast<size_t>(pl.units) *
                                             (pl.maxp + merge_groups(pl.maxp)) * NCOL * pl.D
