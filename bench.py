@@ -776,8 +776,14 @@ def run_seq_shard(args, ws, rank, local):
         dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start = torch.zeros(1, device=dev)
     with ClockSampler(local) as clk:
         _hold(st)
+        if ws > 1:
+            # a device-side start line: the ranks' GPUs leave this all-reduce
+            # together, so host launch skew between ranks does not show up
+            # as waiting inside the first exchange of the timed region
+            dist.all_reduce(start, async_op=True).wait()
         t0.record(st)
         run_steps(args.steps)
         t1.record(st)
